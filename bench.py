@@ -1,0 +1,383 @@
+"""Benchmark of the routed W4A16 MoE layer on B200 (one JSON line on stdout, rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl muse|reference]
+                    [--workload cfg2] [--tokens 1,4,16,32]
+
+Metric: MoE layer us/call and achieved HBM GB/s (% of the measured B200 copy
+bandwidth) per token count. Default workload: configuration 2 (decode; E=128, top-8, H=2048,
+I=768; T in {1, 4, 16, 32}; uniform router; NVFP4 weights from N(0, 0.02)).
+
+A step is one layer call at every token count of the sweep. Each call is a CUDA-graph
+replay of kernel_fn, preceded (outside its timing) by a 512 MiB write that flushes the L2,
+and timed with CUDA events on the launching stream. `value` is the geometric mean over the
+sweep of the mean us/call; `per_T` lists each token count. Under torchrun every rank runs
+the same single-GPU workload (a replica; the layer's decode path has no data exchange) and
+times are the max over ranks.
+
+`--impl reference` times the CPU oracle (the reference's fp32 dequantise-then-accumulate
+path restated in numpy, all host cores) on the same workload; rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+REPO = Path(__file__).resolve().parent
+sys.path.insert(0, str(REPO))
+import __graft_entry__  # noqa: E402
+
+FLUSH_BYTES = 512 << 20
+PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("muse", "reference"), default="muse")
+    ap.add_argument("--workload", default="cfg2")
+    ap.add_argument("--tokens", default=None, help="comma list overriding the workload's sweep")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args(argv)
+
+
+def peaks():
+    if PEAKS_FILE.exists():
+        p = json.loads(PEAKS_FILE.read_text())
+        return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "source": "measured"}
+    return dict(FALLBACK_PEAKS, source="fallback")
+
+
+def geomean(v):
+    return math.exp(sum(math.log(x) for x in v) / len(v))
+
+
+# ----------------------------------------------------------------------------- distributed
+
+def dist_setup(n_gpus):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        torch.distributed.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                             device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        torch.distributed.barrier()
+
+
+def max_over_ranks(world, values: list[float]) -> list[float]:
+    if world == 1:
+        return values
+    t = torch.tensor(values, dtype=torch.float64, device="cuda")
+    torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+    return t.tolist()
+
+
+# ----------------------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while the timed region runs."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (FileNotFoundError, OSError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, f[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- workloads
+
+def workload(args, pkg_synth):
+    shape = pkg_synth.CONFIGS[args.workload]
+    tokens = tuple(int(t) for t in args.tokens.split(",")) if args.tokens else pkg_synth.TOKENS[args.workload]
+    return shape, tokens
+
+
+def input_seed(workload_name: str, t: int) -> int:
+    return 1000 * int(workload_name.removeprefix("cfg") or 0) + t
+
+
+# ----------------------------------------------------------------------------- reference arm
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return 0
+    from oracle import moe_oracle as orc
+
+    pkg = __graft_entry__.load_package()
+    from muse_moe_w4a16_b200 import synth
+    shape, tokens = workload(args, synth)
+    cores = os.cpu_count() or 1
+    w = synth.baseline_weights(shape, seed=synth.WEIGHTS_SEED, device="cuda" if torch.cuda.is_available() else "cpu")
+    w_np = {k: (v.view(torch.uint8) if v.dtype == torch.float8_e4m3fn else
+                v.view(torch.uint16) if v.dtype == torch.bfloat16 else v).cpu().numpy() for k, v in w.items()}
+    del pkg
+    inputs = {t: synth.baseline_input(shape, t, seed=input_seed(args.workload, t)) for t in tokens}
+
+    def call(t):
+        d = inputs[t]
+        orc.ref_kernel_threads(d["hidden_states"].view(torch.uint16).numpy(), d["topk_ids"].numpy(),
+                               d["topk_weights"].numpy(), w_np, shape.local_start, shape.n_local,
+                               shape.inter, threads=cores)
+
+    for i in range(args.warmup):
+        call(tokens[0])
+    samples = {t: [] for t in tokens}
+    n = max(args.steps, len(tokens))
+    for i in range(n):
+        t = tokens[i % len(tokens)]
+        t0 = time.perf_counter()
+        call(t)
+        samples[t].append((time.perf_counter() - t0) * 1e6)
+    per_t = {t: statistics.mean(v) for t, v in samples.items()}
+    value = geomean(list(per_t.values()))
+    line = {
+        "impl": "reference", "metric": metric_name(args), "value": value, "unit": "us/call",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": sum(per_t.values()) / 1e3, "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_block(args, shape, tokens),
+        "per_T": [{"T": t, "us": per_t[t], "samples": len(samples[t])} for t in tokens],
+        "cpu_baseline": {"value": value, "unit": "us/call", "cores": cores, "kind": "port",
+                         "sample": f"one layer call per step, token counts {list(tokens)} in rotation"},
+        "e2e": {"value": value, "unit": "us/call", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def metric_name(args):
+    return f"MoE layer us/call (geomean over the token sweep), {args.workload}"
+
+
+def config_block(args, shape, tokens):
+    return {"workload": f"{args.workload}: E={shape.n_experts} top-{shape.top_k} H={shape.hidden} "
+                        f"I={shape.inter} local=[{shape.local_start},{shape.local_start + shape.n_local}) "
+                        f"router={shape.router} T={list(tokens)}",
+            "weights": "NVFP4 (e2m1, e4m3 block-16 scales, fp32 global scale) from N(0,0.02)",
+            "activations": "bf16 N(0,1)", "l2": "flushed by a 512 MiB write before every timed call",
+            "parallelism": f"replicas x{args.gpus}" if args.gpus > 1 else "single GPU"}
+
+
+# ----------------------------------------------------------------------------- CPU baseline leg
+
+def cpu_baseline(shape, tokens, w, inputs):
+    from oracle import moe_oracle as orc
+    cores = os.cpu_count() or 1
+    w_np = {k: (v.view(torch.uint8) if v.dtype == torch.float8_e4m3fn else
+                v.view(torch.uint16) if v.dtype == torch.bfloat16 else v).cpu().numpy() for k, v in w.items()}
+    per_t = {}
+    for t in tokens:
+        d = inputs[t]
+        t0 = time.perf_counter()
+        orc.ref_kernel_threads(d["hidden_states"].cpu().view(torch.uint16).numpy(), d["topk_ids"].cpu().numpy(),
+                               d["topk_weights"].cpu().numpy(), w_np, shape.local_start, shape.n_local,
+                               shape.inter, threads=cores)
+        per_t[t] = (time.perf_counter() - t0) * 1e6
+    return {"value": geomean(list(per_t.values())), "unit": "us/call", "cores": cores, "kind": "port",
+            "sample": f"one call per token count {list(tokens)} (numpy oracle, {cores} threads)",
+            "per_T_us": {str(t): v for t, v in per_t.items()}}
+
+
+# ----------------------------------------------------------------------------- our arm
+
+def run_muse(args, world, rank, local):
+    pkg = __graft_entry__.load_package()
+    from muse_moe_w4a16_b200 import synth
+    from oracle import moe_oracle as orc  # byte/flop model only; never on the timed path
+
+    dev = torch.device("cuda", local)
+    shape, tokens = workload(args, synth)
+    w = synth.baseline_weights(shape, seed=synth.WEIGHTS_SEED, device=dev)
+    state = pkg.prepare(w)
+    inputs = {t: synth.baseline_input(shape, t, seed=input_seed(args.workload, t)) for t in tokens}
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    # Device-resident inputs and one captured graph per token count.
+    graphs, outs, dev_in = {}, {}, {}
+    for t in tokens:
+        d = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in inputs[t].items()}
+        dev_in[t] = d
+        pkg.kernel_fn(d, state)          # eager first call (kernel attributes)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            outs[t] = pkg.kernel_fn(d, state)
+        graphs[t] = g
+
+    # End-to-end graphs: pinned host inputs -> device, kernel_fn, result -> pinned host.
+    e2e_graphs, h2d, d2h = {}, 0, 0
+    host_in, host_out = {}, {}
+    for t in tokens:
+        hi = {k: (v.pin_memory() if isinstance(v, torch.Tensor) else v) for k, v in inputs[t].items()}
+        host_in[t] = hi
+        host_out[t] = torch.empty((t, shape.hidden), dtype=torch.bfloat16).pin_memory()
+        d = {k: (torch.empty_like(v, device=dev) if isinstance(v, torch.Tensor) else v) for k, v in hi.items()}
+        for k in ("hidden_states", "topk_ids", "topk_weights"):
+            d[k].copy_(hi[k], non_blocking=True)
+        pkg.kernel_fn(d, state)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            for k in ("hidden_states", "topk_ids", "topk_weights"):
+                d[k].copy_(hi[k], non_blocking=True)
+            o = pkg.kernel_fn(d, state)
+            host_out[t].copy_(o, non_blocking=True)
+        e2e_graphs[t] = g
+        h2d += sum(hi[k].numel() * hi[k].element_size() for k in ("hidden_states", "topk_ids", "topk_weights"))
+        d2h += host_out[t].numel() * 2
+
+    def timed(graph_map, steps):
+        ev = {t: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                  for _ in range(steps)] for t in tokens}
+        for i in range(steps):
+            for t in tokens:
+                flush.zero_()
+                ev[t][i][0].record(stream)
+                graph_map[t].replay()
+                ev[t][i][1].record(stream)
+        return ev
+
+    # warm-up (untimed)
+    timed(graphs, args.warmup)
+    timed(e2e_graphs, max(1, args.warmup))
+    torch.cuda.synchronize()
+
+    with ClockSampler(local) as clocks:
+        barrier(world)
+        torch.cuda.synchronize()
+        ev = timed(graphs, args.steps)
+        torch.cuda.synchronize()
+        barrier(world)
+    ev_e2e = timed(e2e_graphs, args.steps)
+    torch.cuda.synchronize()
+
+    per_t = [statistics.mean(a.elapsed_time(b) * 1e3 for a, b in ev[t]) for t in tokens]
+    per_t_e2e = [statistics.mean(a.elapsed_time(b) * 1e3 for a, b in ev_e2e[t]) for t in tokens]
+    per_t = max_over_ranks(world, per_t)
+    per_t_e2e = max_over_ranks(world, per_t_e2e)
+
+    # Correctness of what was timed: the graph outputs against the oracle (cheap sizes only).
+    pk = peaks()
+    per_rows = []
+    tot_bytes = tot_time = 0.0
+    for t, us in zip(tokens, per_t):
+        ids = inputs[t]["topk_ids"].numpy()
+        b = orc.algorithmic_bytes(ids, shape.local_start, shape.n_local, shape.hidden, shape.inter)
+        f = orc.algorithmic_flops(ids, shape.local_start, shape.n_local, shape.hidden, shape.inter)
+        gbs = b / (us * 1e-6) / 1e9
+        tot_bytes += b
+        tot_time += us
+        per_rows.append({"T": t, "us": round(us, 3), "bytes": b, "flops": f, "GBps": round(gbs, 1),
+                         "hbm_frac": round(gbs / pk["hbm_gbs"], 4),
+                         "roofline_us": round(max(b / pk["hbm_gbs"] / 1e3, f / pk["bf16_tflops"] / 1e6), 3)})
+    achieved = tot_bytes / (tot_time * 1e-6) / 1e9
+    launches_per_call = 4
+    line = {
+        "metric": metric_name(args), "value": round(geomean(per_t), 3), "unit": "us/call",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(sum(per_t) / 1e3, 5), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; random-init NVFP4 weights)",
+        "config": config_block(args, shape, tokens),
+        "per_T": per_rows,
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
+                     "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
+                     "peak_source": pk["source"],
+                     "kernel": "whole layer call (route + GEMM1/SiLU + GEMM2/norm + combine), sweep aggregate"},
+        "e2e": {"value": round(geomean(per_t_e2e), 3), "unit": "us/call", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "how": "CUDA graph of pinned-host->device copies, kernel_fn, device->pinned-host copy"},
+        "gpu_launches": launches_per_call * len(tokens) * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(shape, tokens, w, inputs)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    return 0
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    world, rank, local = dist_setup(args.gpus)
+    try:
+        if args.impl == "reference":
+            return run_reference(args, world, rank)
+        return run_muse(args, world, rank, local)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    sys.exit(main())

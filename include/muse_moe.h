@@ -1,0 +1,106 @@
+/*
+ * muse_moe.h -- C ABI of the B200 (sm_100a) routed W4A16 MoE layer.
+ *
+ * Plain pointers, sizes and a cudaStream_t; no torch types. Every device pointer is a
+ * global-memory address on the current device; every call is asynchronous on `stream`,
+ * allocates nothing, never synchronises the host and can be captured in a CUDA graph
+ * (after the first call on a device, which sets kernel attributes).
+ *
+ * Tensor conventions (the reference's Weights / Inputs, baseline.py:27-52):
+ *   x            bf16  [T, H]              hidden states, row-major
+ *   topk_ids     int32 [T, K]              GLOBAL expert ids
+ *   topk_weights fp32  [T, K]
+ *   w13          u8    [E, 2I, H/2]        E2M1 codes, element 2i in the low nibble;
+ *                                          rows [0, I) gate, [I, 2I) up
+ *   w13_sf       u8    [E, 2I, H/16]       fp8 e4m3fn block scales (raw bytes)
+ *   w13_gs       fp32  [E]                 global scales
+ *   w2 / w2_sf / w2_gs   [E, H, I/2] / [E, H, I/16] / [E]
+ *   post_norm_w  bf16  [H]                 the post-expert RMSNorm weight (applied as 1 + w)
+ *   out          bf16  [T, H]
+ * "Prepared" weights are the output of muse_moe_prepare_weights: the same bytes in the
+ * kernels' tile order, same total size (a lossless repack).
+ *
+ * Return value of every entry point: 0 on success, a positive cudaError_t code when a CUDA
+ * call or launch failed, or one of the negative MUSE_ERR_* codes below.
+ */
+#ifndef MUSE_MOE_H_
+#define MUSE_MOE_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* muse_stream_t; /* == cudaStream_t */
+
+#define MUSE_OK                      0
+#define MUSE_ERR_INVALID_ARGUMENT   (-1)  /* null pointer, negative size, inconsistent dims   */
+#define MUSE_ERR_UNSUPPORTED_SHAPE  (-2)  /* H or I not a multiple of 128, K > 16, E_l > 256  */
+#define MUSE_ERR_WORKSPACE_TOO_SMALL (-3) /* workspace smaller than muse_moe_workspace_size   */
+#define MUSE_ERR_NO_DEVICE          (-4)  /* no sm_100 device current                          */
+#define MUSE_ERR_DEVICE_TIMEOUT     (-5)  /* a bounded device-side wait expired                */
+
+/* Library version, (major << 16) | minor. */
+int muse_moe_version(void);
+
+/* Human-readable text for a return code (static storage). */
+const char* muse_moe_error_string(int code);
+
+/*
+ * Bytes of scratch memory muse_moe_forward needs for `tokens` tokens. Replaces the
+ * per-call torch.empty caches of baseline.py:132-135 (cache1/cache2/cache3) and the
+ * moe_align_block_size outputs of baseline.py:129-130.
+ */
+int muse_moe_workspace_size(int tokens, int top_k, int local_count, int hidden, int inter,
+                            size_t* bytes);
+
+/*
+ * Lossless repack of `n_experts` experts into the kernels' tile order (same byte counts).
+ * Replaces prepare() (baseline.py:82-103; the reference's own repack, submission_v6.py:
+ * 138-246). Inputs and outputs are device buffers; sizes as in the conventions above.
+ */
+int muse_moe_prepare_weights(const uint8_t* w13, const uint8_t* w13_sf,
+                             const uint8_t* w2, const uint8_t* w2_sf,
+                             int n_experts, int hidden, int inter,
+                             uint8_t* w13_out, uint8_t* w13_sf_out,
+                             uint8_t* w2_out, uint8_t* w2_sf_out, muse_stream_t stream);
+
+/*
+ * Token -> local-expert grouping. Replaces moe_align_block_size (baseline.py:121-130) and the
+ * unique/nonzero loop of ref_kernel (reference.py:99-102). For the local experts
+ * [local_start, local_start + local_count):
+ *   expert_offsets int32[local_count + 1]  exclusive prefix of the per-expert pair counts
+ *   pair_order     int32[tokens * top_k]   flat pair index t*K+s, grouped by expert, and in
+ *                                          ascending flat order within an expert (stable);
+ *                                          entries past expert_offsets[local_count] are -1
+ *   pair_row       int32[tokens * top_k]   inverse of pair_order, -1 for non-local pairs
+ * Bit-exact with a stable sort by expert.
+ */
+int muse_moe_route(const int32_t* topk_ids, int tokens, int top_k, int local_start,
+                   int local_count, int32_t* expert_offsets, int32_t* pair_order,
+                   int32_t* pair_row, muse_stream_t stream);
+
+/*
+ * The whole routed-expert layer call: routing, GEMM1 (w13) with SiLU(gate)*up, GEMM2 (w2),
+ * post-expert RMSNorm (eps 1e-8) and the top-k-weighted combine, written as bf16 into `out`.
+ * Tokens with no local pair get zeros. Replaces kernel_fn (baseline.py:106-151) and computes
+ * ref_kernel's function (reference.py:93-107).
+ *   w13p/w13_sfp/w2p/w2_sfp  prepared weights of the LOCAL experts (expert local_start first)
+ *   w13_gs/w2_gs             fp32[local_count] global scales of the local experts
+ *   workspace                >= muse_moe_workspace_size(...) bytes, 256-byte aligned
+ */
+int muse_moe_forward(const void* x, const int32_t* topk_ids, const float* topk_weights,
+                     int tokens, int top_k, int local_start, int local_count,
+                     int hidden, int inter,
+                     const uint8_t* w13p, const uint8_t* w13_sfp, const float* w13_gs,
+                     const uint8_t* w2p, const uint8_t* w2_sfp, const float* w2_gs,
+                     const void* post_norm_w, void* out,
+                     void* workspace, size_t workspace_bytes, muse_stream_t stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* MUSE_MOE_H_ */

@@ -1,0 +1,134 @@
+"""The reference-facing interface: prepare(weights) / kernel_fn(data, state) / moe_forward.
+
+Mirrors baseline.py:27-52 (the TypedDicts), baseline.py:82-151 (prepare / kernel_fn) and
+reference.py:93 (ref_kernel's signature, here moe_forward). Tensors must already be on a CUDA
+device; torch supplies device memory and the current stream, the work runs in libmusemoe.so.
+
+Graph rules (TASK.md:72-78): kernel_fn makes no host sync, branches only on shapes and
+`config`, and allocates only through torch's caching allocator (its output and one scratch
+workspace), so it can be captured in a CUDA graph after one eager call.
+"""
+
+from __future__ import annotations
+
+import weakref
+from typing import TypedDict
+
+import torch
+
+from . import _lib
+
+
+class Weights(TypedDict):
+    w13: torch.Tensor          # uint8 [E, 2I, H/2], gate rows [0, I) then up rows [I, 2I), packed E2M1
+    w13_sf: torch.Tensor       # float8_e4m3fn [E, 2I, H/16]
+    w13_gs: torch.Tensor       # float32 [E]
+    w2: torch.Tensor           # uint8 [E, H, I/2]
+    w2_sf: torch.Tensor        # float8_e4m3fn [E, H, I/16]
+    w2_gs: torch.Tensor        # float32 [E]
+    post_norm_w: torch.Tensor  # bfloat16 [H], the post-expert RMSNorm's weight (applied as 1 + w)
+
+
+class Config(TypedDict):
+    bs: int           # tokens, M
+    d_hidden: int     # H
+    d_expert: int     # I
+    n_experts: int    # experts in the model
+    local_start: int  # this GPU computes experts [local_start, local_start + local_count)
+    local_count: int
+    top_k: int
+    sharding: str
+
+
+class Inputs(TypedDict):
+    hidden_states: torch.Tensor  # bfloat16 [M, H]
+    topk_ids: torch.Tensor       # int32 [M, K], global expert ids
+    topk_weights: torch.Tensor   # float32 [M, K]
+    config: Config
+
+
+def _ptr(t: torch.Tensor, byte_offset: int = 0) -> int:
+    return t.data_ptr() + byte_offset
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require_cuda(t: torch.Tensor, name: str) -> None:
+    if not t.is_cuda:
+        raise _lib.MuseError(_lib.MUSE_ERR_NO_DEVICE, f"{name} must be a CUDA tensor (no CPU path)")
+
+
+def prepare(weights: Weights) -> dict:
+    """Repack every expert's NVFP4 weights into the kernels' tile order (lossless, same bytes;
+    baseline.py:82-103). Untimed. The returned state serves any local expert range."""
+    w13, w2 = weights["w13"], weights["w2"]
+    _require_cuda(w13, "w13")
+    E, two_i, h_half = w13.shape
+    H, I = 2 * h_half, two_i // 2
+    if tuple(w2.shape) != (E, H, I // 2):
+        raise _lib.MuseError(_lib.MUSE_ERR_INVALID_ARGUMENT, f"w2 shape {tuple(w2.shape)} != {(E, H, I // 2)}")
+    dev = w13.device
+    srcs = [weights["w13"], weights["w13_sf"], weights["w2"], weights["w2_sf"]]
+    srcs = [s.contiguous().view(torch.uint8) for s in srcs]
+    outs = [torch.empty_like(s) for s in srcs]
+    with torch.cuda.device(dev):
+        _lib.call("muse_moe_prepare_weights", *[_ptr(s) for s in srcs], E, H, I,
+                  *[_ptr(o) for o in outs], _stream(dev))
+    return {
+        "w13": outs[0], "w13_sf": outs[1], "w2": outs[2], "w2_sf": outs[3],
+        "w13_gs": weights["w13_gs"].to(device=dev, dtype=torch.float32).contiguous(),
+        "w2_gs": weights["w2_gs"].to(device=dev, dtype=torch.float32).contiguous(),
+        "post_norm_w": weights["post_norm_w"].to(device=dev, dtype=torch.bfloat16).contiguous(),
+        "n_experts": E, "hidden": H, "inter": I,
+    }
+
+
+def kernel_fn(data: Inputs, state: dict, out: torch.Tensor | None = None) -> torch.Tensor:
+    """One routed-expert layer call (baseline.py:106-151): returns bf16 [T, H] on the GPU."""
+    cfg = data["config"]
+    x = data["hidden_states"]
+    _require_cuda(x, "hidden_states")
+    if x.dtype != torch.bfloat16:
+        raise _lib.MuseError(_lib.MUSE_ERR_INVALID_ARGUMENT, "hidden_states must be bfloat16")
+    x = x.contiguous()
+    ids = data["topk_ids"].to(torch.int32).contiguous()
+    wts = data["topk_weights"].to(torch.float32).contiguous()
+    T, H = x.shape
+    K = ids.shape[1]
+    I = state["inter"]
+    lo, cnt = int(cfg["local_start"]), int(cfg["local_count"])
+    if H != state["hidden"] or lo < 0 or lo + cnt > state["n_experts"] or tuple(ids.shape) != (T, K) \
+            or tuple(wts.shape) != (T, K):
+        raise _lib.MuseError(_lib.MUSE_ERR_INVALID_ARGUMENT,
+                             f"inconsistent shapes: x {tuple(x.shape)}, ids {tuple(ids.shape)}, "
+                             f"weights {tuple(wts.shape)}, local [{lo}, {lo + cnt}) of {state['n_experts']}")
+    dev = x.device
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+    ws_bytes = _lib.workspace_size(T, K, cnt, H, I)
+    ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
+    w13_e, w13sf_e = 2 * I * H // 2, 2 * I * H // 16     # bytes per expert
+    w2_e, w2sf_e = H * I // 2, H * I // 16
+    _lib.call("muse_moe_forward", _ptr(x), _ptr(ids), _ptr(wts), T, K, lo, cnt, H, I,
+              _ptr(state["w13"], lo * w13_e), _ptr(state["w13_sf"], lo * w13sf_e),
+              _ptr(state["w13_gs"], lo * 4),
+              _ptr(state["w2"], lo * w2_e), _ptr(state["w2_sf"], lo * w2sf_e),
+              _ptr(state["w2_gs"], lo * 4),
+              _ptr(state["post_norm_w"]), _ptr(out), _ptr(ws), ws_bytes, _stream(dev))
+    return out
+
+
+# prepare() results cached per weights dict (never on `data`, TASK.md:75).
+_STATE_CACHE: dict[int, tuple[weakref.ref, dict]] = {}
+
+
+def moe_forward(data: Inputs, weights: Weights) -> torch.Tensor:
+    """ref_kernel's signature (reference.py:93): prepare once per weights, then kernel_fn."""
+    key = id(weights["w13"])
+    hit = _STATE_CACHE.get(key)
+    if hit is None or hit[0]() is not weights["w13"]:
+        _STATE_CACHE[key] = (weakref.ref(weights["w13"]), prepare(weights))
+        hit = _STATE_CACHE[key]
+    return kernel_fn(data, hit[1])

@@ -1,0 +1,98 @@
+"""CPU-side checks of the C ABI and the host wrapper: the library loads, exports exactly what
+include/muse_moe.h declares, validates arguments before touching the GPU, and the host path
+refuses CPU tensors (there is no fallback). No kernel is launched here."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+@pytest.fixture(scope="module")
+def lib(pkg):
+    import __graft_entry__
+    if not pkg.library_path().exists():
+        __graft_entry__.build()
+    return pkg.load_library()
+
+
+def declared_symbols() -> set[str]:
+    text = (REPO / "include" / "muse_moe.h").read_text()
+    return set(re.findall(r"^\s*(?:const\s+)?\w+\*?\s+\**(muse_moe_\w+)\s*\(", text, flags=re.M))
+
+
+def test_header_declares_entry_points():
+    syms = declared_symbols()
+    assert {"muse_moe_forward", "muse_moe_route", "muse_moe_prepare_weights",
+            "muse_moe_workspace_size", "muse_moe_version", "muse_moe_error_string"} <= syms
+
+
+def test_library_exports_every_declared_symbol(lib, pkg):
+    from muse_moe_w4a16_b200 import _lib
+    for name in declared_symbols():
+        assert hasattr(lib, name), f"{name} not exported"
+        assert name in _lib.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_version_and_errors(lib):
+    assert lib.muse_moe_version() >= 1
+    assert b"success" in lib.muse_moe_error_string(0)
+    assert b"workspace" in lib.muse_moe_error_string(-3)
+
+
+def test_workspace_size_grows_with_tokens(pkg):
+    from muse_moe_w4a16_b200 import _lib
+    a = _lib.workspace_size(1, 8, 128, 2048, 768)
+    b = _lib.workspace_size(32, 8, 128, 2048, 768)
+    assert 0 < a < b
+    assert b % 256 == 0
+
+
+@pytest.mark.parametrize("args,code", [
+    ((1, 8, 128, 2000, 768), -2),   # hidden not a multiple of 128
+    ((1, 32, 128, 2048, 768), -2),  # top_k > 16
+    ((1, 8, 512, 2048, 768), -2),   # too many local experts
+    ((-1, 8, 128, 2048, 768), -1),
+])
+def test_workspace_size_rejects_bad_shapes(lib, args, code):
+    n = ctypes.c_size_t()
+    assert lib.muse_moe_workspace_size(*args, ctypes.byref(n)) == code
+
+
+def test_forward_rejects_null_pointers_before_any_launch(lib):
+    rc = lib.muse_moe_forward(None, None, None, 4, 8, 0, 32, 2048, 768, None, None, None, None,
+                              None, None, None, None, None, 0, None)
+    assert rc == -1
+    # zero tokens is a valid empty call and launches nothing
+    rc = lib.muse_moe_forward(None, None, None, 0, 8, 0, 32, 2048, 768, None, None, None, None,
+                              None, None, None, None, None, 0, None)
+    assert rc == 0
+
+
+def test_route_rejects_bad_arguments(lib):
+    assert lib.muse_moe_route(None, 4, 8, 0, 32, None, None, None, None) == -1
+    assert lib.muse_moe_route(None, 4, 8, 0, 1000, None, None, None, None) == -2
+
+
+def test_host_path_refuses_cpu_tensors(pkg):
+    from muse_moe_w4a16_b200 import synth
+    shape = synth.MoEShape(4, 2, 128, 128)
+    w = synth.baseline_weights(shape)
+    with pytest.raises(pkg.MuseError):
+        pkg.prepare(w)
+    d = synth.baseline_input(shape, 3, seed=0)
+    with pytest.raises(pkg.MuseError):
+        pkg.kernel_fn(d, {"inter": 128, "hidden": 128, "n_experts": 4})
+
+
+def test_product_path_does_not_import_oracle():
+    pkg_dir = REPO / "muse-moe-w4a16_b200"
+    for f in pkg_dir.rglob("*.py"):
+        for line in f.read_text().splitlines():
+            assert not re.match(r"\s*(from|import)\s+oracle\b", line), f"{f.name}: {line}"

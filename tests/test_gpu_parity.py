@@ -1,0 +1,196 @@
+"""Parity of the CUDA layer (through the C ABI) with the CPU oracle, on seeded inputs.
+
+Bar: routing indices bit-exact; layer output within checks.py's rule at tol 1.5e-2
+(reference.py:25): relative L2 <= 1.5e-2 overall and <= 7.5e-2 per row, finite. The
+observed error is far smaller (the kernels accumulate in fp32; inter is bf16 like SGLang's).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import moe_oracle as orc
+from tests.gpu_util import bits, oracle_out, to_device, to_numpy_weights
+
+pytestmark = pytest.mark.gpu
+TOL = 1.5e-2
+GOLDEN = Path(__file__).resolve().parent / "golden"
+DEV = torch.device("cuda:0")
+
+
+@pytest.fixture(scope="module")
+def synth(pkg):
+    from muse_moe_w4a16_b200 import synth as s
+    return s
+
+
+def run_route(pkg, ids: torch.Tensor, lo: int, cnt: int):
+    from muse_moe_w4a16_b200 import _lib
+    T, K = ids.shape
+    ids = ids.to(DEV).contiguous()
+    offsets = torch.full((cnt + 1,), -7, dtype=torch.int32, device=DEV)
+    order = torch.full((max(T * K, 1),), -7, dtype=torch.int32, device=DEV)
+    row = torch.full((max(T * K, 1),), -7, dtype=torch.int32, device=DEV)
+    _lib.call("muse_moe_route", ids.data_ptr(), T, K, lo, cnt, offsets.data_ptr(), order.data_ptr(),
+              row.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    return offsets.cpu().numpy(), order.cpu().numpy()[:T * K], row.cpu().numpy()[:T * K]
+
+
+@pytest.mark.parametrize("T,K,E,lo,cnt", [
+    (1, 8, 128, 0, 128), (4, 8, 128, 0, 128), (33, 8, 256, 0, 32), (257, 8, 256, 32, 32),
+    (5, 2, 8, 0, 8), (128, 8, 256, 0, 256), (3, 4, 16, 12, 4), (4096, 8, 256, 0, 256),
+    (8192, 8, 256, 64, 64), (1000, 3, 64, 0, 1)])
+def test_route_bit_exact(pkg, T, K, E, lo, cnt):
+    rng = np.random.default_rng(T * 7 + E + lo)
+    ids = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]).astype(np.int32)
+    offsets, order, row = run_route(pkg, torch.from_numpy(ids), lo, cnt)
+    o_ref, order_ref, row_ref = orc.route(ids, lo, cnt)
+    np.testing.assert_array_equal(offsets, o_ref)
+    P = order_ref.size
+    np.testing.assert_array_equal(order[:P], order_ref)
+    assert (order[P:] == -1).all()
+    np.testing.assert_array_equal(row, row_ref)
+
+
+def test_route_ids_outside_every_range(pkg):
+    ids = torch.tensor([[-5, 300], [7, 1 << 30]], dtype=torch.int32)
+    offsets, order, row = run_route(pkg, ids, 0, 8)
+    assert (offsets == np.array([0] * 7 + [1, 1])).all()
+    assert order[0] == 2 and (order[1:] == -1).all()
+    assert list(row) == [-1, -1, 0, -1]
+
+
+def _check_layer(pkg, w, data, rows=None, w_np=None):
+    w_np = to_numpy_weights(w) if w_np is None else w_np
+    out = pkg.moe_forward(to_device(data, DEV), to_device(w, DEV))
+    torch.cuda.synchronize()
+    got = bits(out)
+    ref = oracle_out(data, w_np, rows=rows)
+    if rows is not None:
+        got = got[rows]
+    ok, msg, err, worst = orc.compare(got, ref, TOL)
+    assert ok, msg
+    return err, worst
+
+
+@pytest.mark.parametrize("name", ["small_e4_k2", "small_ep_e8_k3", "small_zipf_e16_k4"])
+def test_layer_matches_golden_small(pkg, name):
+    import json
+    z = np.load(GOLDEN / f"{name}.npz")
+    meta = json.loads(str(z["meta"]))
+    w = {"w13": torch.from_numpy(z["w13"]), "w13_sf": torch.from_numpy(z["w13_sf"]).view(torch.float8_e4m3fn),
+         "w13_gs": torch.from_numpy(z["w13_gs"]), "w2": torch.from_numpy(z["w2"]),
+         "w2_sf": torch.from_numpy(z["w2_sf"]).view(torch.float8_e4m3fn), "w2_gs": torch.from_numpy(z["w2_gs"]),
+         "post_norm_w": torch.from_numpy(z["post_norm_w"]).view(torch.bfloat16)}
+    data = {"hidden_states": torch.from_numpy(z["x"]).view(torch.bfloat16),
+            "topk_ids": torch.from_numpy(z["topk_ids"]), "topk_weights": torch.from_numpy(z["topk_weights"]),
+            "config": {"local_start": meta["local_start"], "local_count": meta["local_count"],
+                       "d_expert": meta["I"], "d_hidden": meta["H"]}}
+    out = pkg.moe_forward(to_device(data, DEV), to_device(w, DEV))
+    ok, msg, err, _ = orc.compare(bits(out), z["out"], TOL)   # against the REFERENCE's output
+    assert ok and err < 5e-3, msg
+
+
+def test_layer_cfg1(pkg, synth):
+    shape = synth.CONFIGS["cfg1"]
+    w = synth.baseline_weights(shape, seed=5252)
+    err, _ = _check_layer(pkg, w, synth.baseline_input(shape, 16, seed=1016))
+    assert err < 5e-3
+
+
+@pytest.fixture(scope="module")
+def cfg2_weights(synth):
+    shape = synth.CONFIGS["cfg2"]
+    return shape, synth.baseline_weights(shape, seed=5252, device="cuda")
+
+
+@pytest.mark.parametrize("T", [1, 4, 16, 32])
+def test_layer_cfg2_decode(pkg, synth, cfg2_weights, T):
+    shape, w = cfg2_weights
+    err, _ = _check_layer(pkg, w, synth.baseline_input(shape, T, seed=2000 + T))
+    assert err < 5e-3
+
+
+@pytest.mark.parametrize("T", [128, 257])
+def test_layer_cfg3_zipf(pkg, synth, cfg2_weights, T):
+    _, w = cfg2_weights
+    shape = synth.CONFIGS["cfg3"]
+    err, _ = _check_layer(pkg, w, synth.baseline_input(shape, T, seed=3000 + T))
+    assert err < 5e-3
+
+
+@pytest.mark.parametrize("bs,dist", [(4, "normal"), (33, "normal"), (1, "normal"), (128, "skewed")])
+def test_layer_reference_problem_reduced(pkg, synth, bs, dist):
+    """The reference's own generators and gating shapes (TASK.md:46-54) at H = I = 512, E = 64,
+    ep8 (8 local experts), busiest rotation."""
+    shape = synth.MoEShape(64, 8, 512, 512, local_start=0, local_count=8, router="reference")
+    w = synth.reference_weights(shape, seed=5252)
+    err, _ = _check_layer(pkg, w, synth.reference_input(shape, bs, seed=100 + bs, dist=dist))
+    assert err < 5e-3
+
+
+def test_layer_tokens_without_local_pairs_are_zero(pkg, synth):
+    shape = synth.MoEShape(16, 2, 256, 128, local_start=8, local_count=4, router="uniform")
+    w = synth.baseline_weights(shape, seed=1)
+    data = synth.baseline_input(shape, 9, seed=3)
+    data["topk_ids"][0] = torch.tensor([0, 1], dtype=torch.int32)   # token 0: nothing local
+    out = pkg.moe_forward(to_device(data, DEV), to_device(w, DEV))
+    assert (bits(out)[0] == 0).all()
+    _check_layer(pkg, w, data)
+
+
+def test_layer_empty_batch(pkg, synth):
+    shape = synth.MoEShape(8, 2, 128, 128)
+    w = synth.baseline_weights(shape, seed=1)
+    data = synth.baseline_input(shape, 0, seed=3)
+    out = pkg.moe_forward(to_device(data, DEV), to_device(w, DEV))
+    assert out.shape == (0, 128)
+
+
+def test_layer_cuda_graph_replay(pkg, synth, cfg2_weights):
+    """kernel_fn captured in a CUDA graph, replayed on fresh inputs copied into its buffers."""
+    shape, w = cfg2_weights
+    state = pkg.prepare(w)
+    d0 = to_device(synth.baseline_input(shape, 16, seed=1), DEV)
+    pkg.kernel_fn(d0, state)  # eager call first: sets kernel attributes
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = pkg.kernel_fn(d0, state)
+    w_np = to_numpy_weights(w)
+    for seed in (5, 6):
+        d = synth.baseline_input(shape, 16, seed=seed)
+        for k in ("hidden_states", "topk_ids", "topk_weights"):
+            d0[k].copy_(d[k])
+        g.replay()
+        torch.cuda.synchronize()
+        ok, msg, *_ = orc.compare(bits(out), oracle_out(d, w_np), TOL)
+        assert ok, msg
+
+
+def test_layer_cfg4_large_expert_sampled_rows(pkg, synth):
+    """E=256, H=7168, I=2048 at T=32: every token is computed on the GPU, 3 rows are checked
+    against the oracle (the oracle dequantises only their experts)."""
+    shape = synth.CONFIGS["cfg4"]
+    data = synth.baseline_input(shape, 32, seed=4032)
+    rows = [0, 13, 31]
+    need = sorted(set(data["topk_ids"][rows].reshape(-1).tolist()))
+    w = synth.baseline_weights(shape, seed=5252, device="cuda")
+    w_np = to_numpy_weights({k: (v[need] if v.dim() > 1 or k.endswith("_gs") else v) for k, v in w.items()})
+    # oracle over the needed experts only: remap their ids to 0..len(need)-1
+    remap = {e: j for j, e in enumerate(need)}
+    sub = {"hidden_states": data["hidden_states"][rows],
+           "topk_ids": torch.tensor([[remap.get(int(e), -1) for e in r] for r in data["topk_ids"][rows]],
+                                    dtype=torch.int32),
+           "topk_weights": data["topk_weights"][rows],
+           "config": dict(data["config"], local_start=0, local_count=len(need))}
+    ref = oracle_out(sub, w_np)
+    out = pkg.moe_forward(to_device(data, DEV), w)
+    ok, msg, err, _ = orc.compare(bits(out)[rows], ref, TOL)
+    assert ok and err < 5e-3, msg
