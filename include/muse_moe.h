@@ -57,6 +57,22 @@ int muse_moe_workspace_size(int tokens, int top_k, int local_count, int hidden, 
                             size_t* bytes);
 
 /*
+ * Byte offsets of the scratch buffers inside the workspace, for inspection by tests:
+ * offsets[0..7] = expert_offsets, pair_order, pair_row, xs (bf16 [T*K, H] gathered hidden
+ * states), inter (bf16 [T*K, I]), ypart (fp32 [T*K, H]), ssq (fp32 [T*K]), total bytes.
+ * Rows of xs / inter / ypart / ssq are in pair_order order.
+ */
+int muse_moe_workspace_offsets(int tokens, int top_k, int local_count, int hidden, int inter,
+                               size_t* offsets);
+
+/*
+ * Sticky per-device status word of the kernels' bounded waits: 0, or the code of the first
+ * role whose wait expired (then a call returned garbage). Synchronous: copies from the device
+ * on the current device; reset != 0 clears it. Not for use inside a captured graph.
+ */
+int muse_moe_device_status(int* status, int reset);
+
+/*
  * Lossless repack of `n_experts` experts into the kernels' tile order (same byte counts).
  * Replaces prepare() (baseline.py:82-103; the reference's own repack, submission_v6.py:
  * 138-246). Inputs and outputs are device buffers; sizes as in the conventions above.

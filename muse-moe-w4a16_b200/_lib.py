@@ -20,6 +20,8 @@ SIGNATURES: dict[str, tuple] = {
     "muse_moe_version": (_I, []),
     "muse_moe_error_string": (ctypes.c_char_p, [_I]),
     "muse_moe_workspace_size": (_I, [_I, _I, _I, _I, _I, _SIZE_P]),
+    "muse_moe_workspace_offsets": (_I, [_I, _I, _I, _I, _I, _SIZE_P]),
+    "muse_moe_device_status": (_I, [ctypes.POINTER(ctypes.c_int), _I]),
     "muse_moe_prepare_weights": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P]),
     "muse_moe_route": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P]),
     "muse_moe_forward": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I,
@@ -82,6 +84,21 @@ def check(rc: int) -> None:
 def call(name: str, *args) -> None:
     """Call an int-returning entry point and raise on failure."""
     check(getattr(load_library(), name)(*args))
+
+
+def workspace_offsets(tokens: int, top_k: int, local_count: int, hidden: int, inter: int) -> dict:
+    """Byte offsets of the scratch buffers inside the workspace (include/muse_moe.h)."""
+    arr = (ctypes.c_size_t * 8)()
+    call("muse_moe_workspace_offsets", tokens, top_k, local_count, hidden, inter, arr)
+    names = ("offsets", "pair_order", "pair_row", "xs", "inter", "ypart", "ssq", "total")
+    return dict(zip(names, (int(v) for v in arr)))
+
+
+def device_status(reset: bool = True) -> int:
+    """The kernels' sticky timeout status on the current device (synchronises)."""
+    st = ctypes.c_int(0)
+    call("muse_moe_device_status", ctypes.byref(st), int(reset))
+    return int(st.value)
 
 
 def workspace_size(tokens: int, top_k: int, local_count: int, hidden: int, inter: int) -> int:

@@ -1,20 +1,31 @@
-// C ABI entry points (include/muse_moe.h): argument validation, workspace carving and the
-// launch sequence of one layer call.
+// C ABI entry points (include/muse_moe.h): argument validation, workspace carving, tensor
+// maps and the launch sequence of one layer call.
+#include <cudaTypedefs.h>
+
 #include "common.cuh"
 #include "kernels.cuh"
+#include "layout.cuh"
 
 namespace muse {
 namespace {
 
 constexpr size_t kAlign = 256;
 
-// Workspace layout for one call; every buffer 256-byte aligned.
+// Workspace layout for one call; every buffer 256-byte aligned. Order of the offsets is the
+// order muse_moe_workspace_offsets reports them in.
 struct WorkspaceLayout {
-  size_t offsets, pair_order, pair_row, inter, ypart, ssq, total;
+  size_t offsets, pair_order, pair_row, xs, inter, ypart, ssq, total;
 };
 
+// Pair-row capacity of the row buffers: at least one full token tile (128 rows), so a TMA box
+// never spans more rows than the tensor map describes.
+size_t pair_rows(int tokens, int top_k) {
+  const size_t p = (size_t)tokens * top_k;
+  return p < 128 ? 128 : p;
+}
+
 WorkspaceLayout workspace_layout(int tokens, int top_k, int local_count, int hidden, int inter) {
-  const size_t P = (size_t)tokens * top_k;
+  const size_t P = pair_rows(tokens, top_k);
   WorkspaceLayout l;
   size_t at = 0;
   auto take = [&](size_t bytes) {
@@ -25,6 +36,7 @@ WorkspaceLayout workspace_layout(int tokens, int top_k, int local_count, int hid
   l.offsets = take(sizeof(int32_t) * (local_count + 1));
   l.pair_order = take(sizeof(int32_t) * P);
   l.pair_row = take(sizeof(int32_t) * P);
+  l.xs = take(2 * P * hidden);
   l.inter = take(2 * P * inter);
   l.ypart = take(4 * P * hidden);
   l.ssq = take(4 * P);
@@ -37,15 +49,47 @@ int check_dims(int tokens, int top_k, int local_start, int local_count, int hidd
     return MUSE_ERR_INVALID_ARGUMENT;
   if (top_k > kMaxTopK || local_count > kMaxLocalExperts || hidden % 128 || inter % 128)
     return MUSE_ERR_UNSUPPORTED_SHAPE;
+  if ((long long)tokens * top_k > (1LL << 30)) return MUSE_ERR_UNSUPPORTED_SHAPE;
   return MUSE_OK;
 }
 
+// Token tile (the MMA's N) from the expected pairs per local expert; shapes only.
+int pick_n_box(int tokens, int top_k, int local_count) {
+  const long long per_expert = 2LL * tokens * top_k / local_count;
+  int n = 16;
+  while (n < 128 && n < per_expert) n <<= 1;
+  return n;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
 }  // namespace
+
+int make_bf16_tmap(CUtensorMap* map, const void* base, int rows, int cols, int box_rows) {
+  if (!g_encode) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess) return e;
+    if (q != cudaDriverEntryPointSuccess || !fn) return MUSE_ERR_NO_DEVICE;
+    g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  const CUresult r = g_encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims,
+                              strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                              CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? MUSE_OK : MUSE_ERR_INVALID_ARGUMENT;
+}
+
 }  // namespace muse
 
 using namespace muse;
 
-extern "C" int muse_moe_version(void) { return (0 << 16) | 1; }
+extern "C" int muse_moe_version(void) { return (0 << 16) | 2; }
 
 extern "C" const char* muse_moe_error_string(int code) {
   switch (code) {
@@ -55,7 +99,7 @@ extern "C" const char* muse_moe_error_string(int code) {
       return "unsupported shape (hidden and inter must be multiples of 128, top_k <= 16, "
              "local_count <= 256)";
     case MUSE_ERR_WORKSPACE_TOO_SMALL: return "workspace smaller than muse_moe_workspace_size()";
-    case MUSE_ERR_NO_DEVICE: return "no sm_100 CUDA device is current";
+    case MUSE_ERR_NO_DEVICE: return "no sm_100 CUDA device / driver entry point available";
     case MUSE_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait expired";
     default: break;
   }
@@ -72,6 +116,22 @@ extern "C" int muse_moe_workspace_size(int tokens, int top_k, int local_count, i
   return MUSE_OK;
 }
 
+extern "C" int muse_moe_workspace_offsets(int tokens, int top_k, int local_count, int hidden,
+                                          int inter, size_t* offsets) {
+  if (!offsets) return MUSE_ERR_INVALID_ARGUMENT;
+  const int rc = check_dims(tokens, top_k, 0, local_count, hidden, inter);
+  if (rc) return rc;
+  const WorkspaceLayout l = workspace_layout(tokens, top_k, local_count, hidden, inter);
+  const size_t v[8] = {l.offsets, l.pair_order, l.pair_row, l.xs, l.inter, l.ypart, l.ssq, l.total};
+  for (int i = 0; i < 8; ++i) offsets[i] = v[i];
+  return MUSE_OK;
+}
+
+extern "C" int muse_moe_device_status(int* status, int reset) {
+  if (!status) return MUSE_ERR_INVALID_ARGUMENT;
+  return read_device_status(status, reset);
+}
+
 extern "C" int muse_moe_prepare_weights(const uint8_t* w13, const uint8_t* w13_sf,
                                         const uint8_t* w2, const uint8_t* w2_sf, int n_experts,
                                         int hidden, int inter, uint8_t* w13_out,
@@ -81,14 +141,14 @@ extern "C" int muse_moe_prepare_weights(const uint8_t* w13, const uint8_t* w13_s
   if (hidden % 128 || inter % 128) return MUSE_ERR_UNSUPPORTED_SHAPE;
   if (!w13 || !w13_sf || !w2 || !w2_sf || !w13_out || !w13_sf_out || !w2_out || !w2_sf_out)
     return MUSE_ERR_INVALID_ARGUMENT;
-  const size_t E = n_experts, H = hidden, I = inter;
+  for (const void* p : {(const void*)w13, (const void*)w13_sf, (const void*)w2, (const void*)w2_sf,
+                        (const void*)w13_out, (const void*)w13_sf_out, (const void*)w2_out,
+                        (const void*)w2_sf_out})
+    if (reinterpret_cast<uintptr_t>(p) % 16) return MUSE_ERR_INVALID_ARGUMENT;
   cudaStream_t s = (cudaStream_t)stream;
-  cudaError_t e;
-  if ((e = cudaMemcpyAsync(w13_out, w13, E * 2 * I * H / 2, cudaMemcpyDeviceToDevice, s))) return e;
-  if ((e = cudaMemcpyAsync(w13_sf_out, w13_sf, E * 2 * I * H / 16, cudaMemcpyDeviceToDevice, s))) return e;
-  if ((e = cudaMemcpyAsync(w2_out, w2, E * H * I / 2, cudaMemcpyDeviceToDevice, s))) return e;
-  if ((e = cudaMemcpyAsync(w2_sf_out, w2_sf, E * H * I / 16, cudaMemcpyDeviceToDevice, s))) return e;
-  return MUSE_OK;
+  int rc = launch_prepare_tiles(w13, w13_sf, n_experts, 2 * inter, hidden, inter, w13_out, w13_sf_out, s);
+  if (rc) return rc;
+  return launch_prepare_tiles(w2, w2_sf, n_experts, hidden, inter, 0, w2_out, w2_sf_out, s);
 }
 
 extern "C" int muse_moe_forward(const void* x, const int32_t* topk_ids, const float* topk_weights,
@@ -104,7 +164,11 @@ extern "C" int muse_moe_forward(const void* x, const int32_t* topk_ids, const fl
   if (!x || !topk_ids || !topk_weights || !w13p || !w13_sfp || !w13_gs || !w2p || !w2_sfp ||
       !w2_gs || !post_norm_w || !out || !workspace)
     return MUSE_ERR_INVALID_ARGUMENT;
-  if (reinterpret_cast<uintptr_t>(workspace) % kAlign) return MUSE_ERR_INVALID_ARGUMENT;
+  if (reinterpret_cast<uintptr_t>(workspace) % kAlign || reinterpret_cast<uintptr_t>(x) % 16 ||
+      reinterpret_cast<uintptr_t>(w13p) % 16 || reinterpret_cast<uintptr_t>(w13_sfp) % 16 ||
+      reinterpret_cast<uintptr_t>(w2p) % 16 || reinterpret_cast<uintptr_t>(w2_sfp) % 16 ||
+      reinterpret_cast<uintptr_t>(out) % 16)
+    return MUSE_ERR_INVALID_ARGUMENT;
   const WorkspaceLayout l = workspace_layout(tokens, top_k, local_count, hidden, inter);
   if (workspace_bytes < l.total) return MUSE_ERR_WORKSPACE_TOO_SMALL;
 
@@ -113,20 +177,60 @@ extern "C" int muse_moe_forward(const void* x, const int32_t* topk_ids, const fl
   s.offsets = reinterpret_cast<int32_t*>(ws + l.offsets);
   s.pair_order = reinterpret_cast<int32_t*>(ws + l.pair_order);
   s.pair_row = reinterpret_cast<int32_t*>(ws + l.pair_row);
-  s.inter = ws + l.inter;
+  s.xs = reinterpret_cast<uint16_t*>(ws + l.xs);
+  s.inter = reinterpret_cast<uint16_t*>(ws + l.inter);
   s.ypart = reinterpret_cast<float*>(ws + l.ypart);
   s.ssq = reinterpret_cast<float*>(ws + l.ssq);
+  if ((rc = device_status_ptr(&s.error_flag))) return rc;
   const LayerDims d{tokens, top_k, local_start, local_count, hidden, inter};
-  const ExpertWeights w{w13p, w13_sfp, w13_gs, w2p, w2_sfp, w2_gs,
-                        static_cast<const uint16_t*>(post_norm_w)};
+  const int P = d.n_pairs();
+  const int rows = (int)pair_rows(tokens, top_k);
+  const int n_box = pick_n_box(tokens, top_k, local_count);
+  const int stages = pick_stages(n_box);
   cudaStream_t st = (cudaStream_t)stream;
 
-  cudaError_t ce = cudaMemsetAsync(s.ssq, 0, sizeof(float) * d.n_pairs(), st);
+  CUtensorMap tmap_x, tmap_i;
+  if ((rc = make_bf16_tmap(&tmap_x, s.xs, rows, hidden, n_box))) return rc;
+  if ((rc = make_bf16_tmap(&tmap_i, s.inter, rows, inter, n_box))) return rc;
+
+  cudaError_t ce = cudaMemsetAsync(s.ssq, 0, sizeof(float) * P, st);
   if (ce != cudaSuccess) return ce;
-  if ((rc = launch_route(topk_ids, tokens, top_k, local_start, local_count, s.offsets,
-                         s.pair_order, s.pair_row, st)))
+  if ((rc = launch_route(topk_ids, tokens, top_k, local_start, local_count, s.offsets, s.pair_order,
+                         s.pair_row, st)))
     return rc;
-  if ((rc = launch_gemm1_silu(d, static_cast<const uint16_t*>(x), w, s, st))) return rc;
-  if ((rc = launch_gemm2_norm(d, w, s, st))) return rc;
+  if ((rc = launch_gather(static_cast<const uint16_t*>(x), s.offsets, s.pair_order, local_count,
+                          top_k, P, hidden, s.xs, st)))
+    return rc;
+
+  GemmArgs g1{};
+  g1.offsets = s.offsets;
+  g1.n_local = local_count;
+  g1.m_tiles = 2 * inter / kTileM;
+  g1.k_chunks = hidden / kChunkK;
+  g1.n_box = n_box;
+  g1.stages = stages;
+  g1.wq = w13p;
+  g1.wsf = w13_sfp;
+  g1.gs = w13_gs;
+  g1.mode = 1;
+  g1.ld_out = inter;
+  g1.inter = s.inter;
+  g1.error_flag = s.error_flag;
+  if ((rc = launch_expert_gemm(tmap_x, g1, st))) return rc;
+
+  GemmArgs g2 = g1;
+  g2.m_tiles = hidden / kTileM;
+  g2.k_chunks = inter / kChunkK;
+  g2.wq = w2p;
+  g2.wsf = w2_sfp;
+  g2.gs = w2_gs;
+  g2.mode = 2;
+  g2.ld_out = hidden;
+  g2.inter = nullptr;
+  g2.post_norm_w = static_cast<const uint16_t*>(post_norm_w);
+  g2.ypart = s.ypart;
+  g2.ssq = s.ssq;
+  if ((rc = launch_expert_gemm(tmap_i, g2, st))) return rc;
+
   return launch_combine(d, topk_ids, topk_weights, s, static_cast<uint16_t*>(out), st);
 }

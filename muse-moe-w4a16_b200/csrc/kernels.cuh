@@ -1,7 +1,9 @@
 // Internal launch interface between the kernel files and the C ABI (abi.cu).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <stddef.h>
 #include <stdint.h>
 
 namespace muse {
@@ -17,12 +19,14 @@ struct Scratch {
   int32_t* offsets;     // [local_count + 1]
   int32_t* pair_order;  // [T*K]
   int32_t* pair_row;    // [T*K]
-  void* inter;          // bf16 [T*K, I]   SiLU(gate)*up per pair, expert-grouped rows
-  float* ypart;         // fp32 [T*K, H]   y * (1 + post_norm_w) per pair
-  float* ssq;           // fp32 [T*K]      sum over H of ypart^2 per pair
+  uint16_t* xs;         // bf16 [T*K, H]  hidden states gathered into expert-grouped pair order
+  uint16_t* inter;      // bf16 [T*K, I]  SiLU(gate)*up per pair, expert-grouped rows
+  float* ypart;         // fp32 [T*K, H]  y * (1 + post_norm_w) per pair
+  float* ssq;           // fp32 [T*K]     sum over H of ypart^2 per pair
+  int* error_flag;      // set by a kernel whose bounded wait expired
 };
 
-// Weights of the local experts, already in the kernels' layout.
+// Weights of the local experts in the prepared (tiled) layout of layout.cuh.
 struct ExpertWeights {
   const uint8_t* w13;
   const uint8_t* w13_sf;
@@ -33,16 +37,49 @@ struct ExpertWeights {
   const uint16_t* post_norm_w;  // bf16 bits
 };
 
+// Arguments of one expert-GEMM launch (gemm_tc.cu).
+struct GemmArgs {
+  const int32_t* offsets;  // [n_local + 1] expert ranges of the pair rows
+  int n_local;
+  int m_tiles;             // weight rows per expert / 128
+  int k_chunks;            // K / 128
+  int n_box;               // token tile = MMA N (16, 32, 64 or 128)
+  int stages;              // shared-memory ring depth
+  const uint8_t* wq;       // prepared codes
+  const uint8_t* wsf;      // prepared scales
+  const float* gs;         // [n_local] global scales
+  int mode;                // 1: SiLU(gate)*up -> inter; 2: post-norm partials -> ypart, ssq
+  int ld_out;              // row length of the output (I in mode 1, H in mode 2)
+  uint16_t* inter;
+  const uint16_t* post_norm_w;
+  float* ypart;
+  float* ssq;
+  int* error_flag;
+};
+
 int launch_route(const int32_t* ids, int tokens, int top_k, int local_start, int local_count,
                  int32_t* offsets, int32_t* pair_order, int32_t* pair_row, cudaStream_t stream);
 
-int launch_gemm1_silu(const LayerDims& d, const uint16_t* x, const ExpertWeights& w,
-                      const Scratch& s, cudaStream_t stream);
+int launch_gather(const uint16_t* x, const int32_t* offsets, const int32_t* pair_order, int n_local,
+                  int top_k, int max_rows, int hidden, uint16_t* xs, cudaStream_t stream);
 
-int launch_gemm2_norm(const LayerDims& d, const ExpertWeights& w, const Scratch& s,
-                      cudaStream_t stream);
+size_t gemm_smem_bytes(int n_box, int stages);
+int pick_stages(int n_box);
+int launch_expert_gemm(const CUtensorMap& tmap_b, const GemmArgs& args, cudaStream_t stream);
+
+// Address of the sticky device status word (current device) and a synchronous read of it.
+int device_status_ptr(int** ptr);
+int read_device_status(int* status, int reset);
 
 int launch_combine(const LayerDims& d, const int32_t* ids, const float* topk_weights,
                    const Scratch& s, uint16_t* out, cudaStream_t stream);
+
+int launch_prepare_tiles(const uint8_t* codes, const uint8_t* scales, int n_experts, int rows,
+                         int k, int gate_up_inter, uint8_t* codes_out, uint8_t* scales_out,
+                         cudaStream_t stream);
+
+// 2-D bf16 tensor map over a row-major [rows, cols] matrix, box = 64 columns x box_rows,
+// 128-byte swizzle, zero fill out of bounds.
+int make_bf16_tmap(CUtensorMap* map, const void* base, int rows, int cols, int box_rows);
 
 }  // namespace muse

@@ -97,7 +97,30 @@ route_kernel(const int32_t* __restrict__ ids, int n_pairs, int lo, int n_local,
   for (int r = total + tid; r < n_pairs; r += kThreads) pair_order[r] = -1;
 }
 
+// xs[r] = x[pair_order[r] / top_k] for the P = offsets[n_local] routed pairs: the GEMM1 B
+// operand in expert-grouped order, so each token tile is a plain 2-D TMA box.
+__global__ void __launch_bounds__(256)
+gather_rows_kernel(const uint16_t* __restrict__ x, const int32_t* __restrict__ offsets,
+                   const int32_t* __restrict__ pair_order, int n_local, int top_k, int hidden,
+                   uint16_t* __restrict__ xs) {
+  const int P = offsets[n_local];
+  const int vec = hidden / 8;
+  for (int r = blockIdx.x; r < P; r += gridDim.x) {
+    const int tok = pair_order[r] / top_k;
+    const uint4* src = reinterpret_cast<const uint4*>(x + (size_t)tok * hidden);
+    uint4* dst = reinterpret_cast<uint4*>(xs + (size_t)r * hidden);
+    for (int i = threadIdx.x; i < vec; i += blockDim.x) dst[i] = src[i];
+  }
+}
+
 }  // namespace
+
+int launch_gather(const uint16_t* x, const int32_t* offsets, const int32_t* pair_order, int n_local,
+                  int top_k, int max_rows, int hidden, uint16_t* xs, cudaStream_t stream) {
+  const int grid = max_rows < 296 ? max_rows : 296;
+  gather_rows_kernel<<<grid, 256, 0, stream>>>(x, offsets, pair_order, n_local, top_k, hidden, xs);
+  return last_launch_status();
+}
 
 int launch_route(const int32_t* ids, int tokens, int top_k, int local_start, int local_count,
                  int32_t* offsets, int32_t* pair_order, int32_t* pair_row, cudaStream_t stream) {

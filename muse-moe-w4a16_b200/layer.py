@@ -85,8 +85,10 @@ def prepare(weights: Weights) -> dict:
     }
 
 
-def kernel_fn(data: Inputs, state: dict, out: torch.Tensor | None = None) -> torch.Tensor:
-    """One routed-expert layer call (baseline.py:106-151): returns bf16 [T, H] on the GPU."""
+def kernel_fn(data: Inputs, state: dict, out: torch.Tensor | None = None,
+              workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """One routed-expert layer call (baseline.py:106-151): returns bf16 [T, H] on the GPU.
+    `out` and `workspace` (uint8, >= workspace_size bytes) may be supplied by the caller."""
     cfg = data["config"]
     x = data["hidden_states"]
     _require_cuda(x, "hidden_states")
@@ -108,7 +110,10 @@ def kernel_fn(data: Inputs, state: dict, out: torch.Tensor | None = None) -> tor
     if out is None:
         out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
     ws_bytes = _lib.workspace_size(T, K, cnt, H, I)
-    ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
+    if workspace is None:
+        ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
+    else:
+        ws, ws_bytes = workspace, workspace.numel() * workspace.element_size()
     w13_e, w13sf_e = 2 * I * H // 2, 2 * I * H // 16     # bytes per expert
     w2_e, w2sf_e = H * I // 2, H * I // 16
     _lib.call("muse_moe_forward", _ptr(x), _ptr(ids), _ptr(wts), T, K, lo, cnt, H, I,

@@ -61,7 +61,7 @@ def test_route_bit_exact(pkg, T, K, E, lo, cnt):
 def test_route_ids_outside_every_range(pkg):
     ids = torch.tensor([[-5, 300], [7, 1 << 30]], dtype=torch.int32)
     offsets, order, row = run_route(pkg, ids, 0, 8)
-    assert (offsets == np.array([0] * 7 + [1, 1])).all()
+    assert (offsets == np.array([0] * 8 + [1])).all()
     assert order[0] == 2 and (order[1:] == -1).all()
     assert list(row) == [-1, -1, 0, -1]
 
@@ -194,3 +194,96 @@ def test_layer_cfg4_large_expert_sampled_rows(pkg, synth):
     out = pkg.moe_forward(to_device(data, DEV), w)
     ok, msg, err, _ = orc.compare(bits(out)[rows], ref, TOL)
     assert ok and err < 5e-3, msg
+
+
+# ----------------------------------------------------------------------------- stage checks
+
+_POS = [(6, 7, 8, 15), (22, 23, 24, 31), (2, 3, 4, 11), (18, 19, 20, 27),
+        (28, 29, 30, 5), (12, 13, 14, 21), (0, 1, 10, 9), (16, 17, 26, 25)]
+
+
+def _unpermute_words(w: np.ndarray) -> np.ndarray:
+    w = w.astype(np.uint64)
+    out = np.zeros_like(w)
+    for k, pos in enumerate(_POS):
+        for b, p in enumerate(pos):
+            out |= ((w >> np.uint64(p)) & np.uint64(1)) << np.uint64(4 * k + b)
+    return out.astype(np.uint32)
+
+
+def _untile(codes: np.ndarray, scales: np.ndarray, E: int, rows: int, k: int, gate_up_inter: int):
+    """Invert the prepared layout (csrc/layout.cuh) back to [E, rows, k/2] / [E, rows, k/16]."""
+    mt, kc = rows // 128, k // 128
+    c = codes.reshape(E, mt, kc, 128, 4, 16)          # [.., row, slot, 16 bytes]
+    s = scales.reshape(E, mt, kc, 128, 8)
+    r = np.arange(128)
+    slot_of_chunk = np.stack([np.arange(4) ^ ((ri >> 1) & 3) for ri in r])   # [128, 4]
+    c = np.take_along_axis(c, slot_of_chunk[None, None, None, :, :, None], axis=4)
+    words = _unpermute_words(c.reshape(-1).view(np.uint32)).view(np.uint8).reshape(c.shape)
+    words = words.reshape(E, mt, kc, 128, 64).transpose(0, 1, 3, 2, 4).reshape(E, mt, 128, k // 2)
+    s = s.transpose(0, 1, 3, 2, 4).reshape(E, mt, 128, k // 16)
+    out_c = np.zeros((E, rows, k // 2), np.uint8)
+    out_s = np.zeros((E, rows, k // 16), np.uint8)
+    for m in range(mt):
+        for ri in range(128):
+            if gate_up_inter:
+                q, i = ri >> 5, ri & 31
+                j = 64 * m + 16 * q + (i & 15)
+                src = j if i < 16 else gate_up_inter + j
+            else:
+                src = 128 * m + ri
+            out_c[:, src] = words[:, m, ri]
+            out_s[:, src] = s[:, m, ri]
+    return out_c, out_s
+
+
+def test_prepare_repack_is_lossless(pkg, synth):
+    shape = synth.MoEShape(3, 2, 256, 384)
+    w = synth.baseline_weights(shape, seed=9)
+    st = pkg.prepare(to_device(w, DEV))
+    torch.cuda.synchronize()
+    H, I = 256, 384
+    c13, s13 = _untile(st["w13"].cpu().numpy(), st["w13_sf"].cpu().numpy(), 3, 2 * I, H, I)
+    np.testing.assert_array_equal(c13, w["w13"].numpy())
+    np.testing.assert_array_equal(s13, w["w13_sf"].view(torch.uint8).numpy())
+    c2, s2 = _untile(st["w2"].cpu().numpy(), st["w2_sf"].cpu().numpy(), 3, H, I, 0)
+    np.testing.assert_array_equal(c2, w["w2"].numpy())
+    np.testing.assert_array_equal(s2, w["w2_sf"].view(torch.uint8).numpy())
+
+
+def test_stage_outputs_match_oracle(pkg, synth):
+    """GEMM1's inter and GEMM2's ypart/ssq, read from the workspace, against fp32 restatements
+    of reference.py:103-106 per pair (inter is stored in bf16)."""
+    from muse_moe_w4a16_b200 import _lib
+    shape = synth.MoEShape(8, 2, 256, 256, router="normal")
+    T, K, H, I = 16, 2, 256, 256
+    w = synth.baseline_weights(shape, seed=5252)
+    d = synth.baseline_input(shape, T, seed=77)
+    st = pkg.prepare(to_device(w, DEV))
+    nbytes = _lib.workspace_size(T, K, 8, H, I)
+    ws = torch.zeros(nbytes, dtype=torch.uint8, device=DEV)
+    pkg.kernel_fn(to_device(d, DEV), st, workspace=ws)
+    torch.cuda.synchronize()
+    assert _lib.device_status() == 0
+    off = _lib.workspace_offsets(T, K, 8, H, I)
+    wsc = ws.cpu()
+    P = T * K
+    order = wsc[off["pair_order"]:off["pair_order"] + 4 * P].view(torch.int32).numpy()
+    inter = wsc[off["inter"]:off["inter"] + 2 * P * I].view(torch.bfloat16).float().numpy().reshape(P, I)
+    ypart = wsc[off["ypart"]:off["ypart"] + 4 * P * H].view(torch.float32).numpy().reshape(P, H)
+    ssq = wsc[off["ssq"]:off["ssq"] + 4 * P].view(torch.float32).numpy()
+    wn = to_numpy_weights(w)
+    x = orc.bf16_to_f32(d["hidden_states"].view(torch.uint16).numpy())
+    ids = d["topk_ids"].numpy()
+    pnw = orc.bf16_to_f32(wn["post_norm_w"])
+    for r, p in enumerate(order):
+        t, s = divmod(int(p), K)
+        e = int(ids[t, s])
+        h = x[t] @ orc.dequantize(wn["w13"][e], wn["w13_sf"][e], wn["w13_gs"][e]).T
+        ref_i = orc.silu(h[:I]) * h[I:]
+        err_i = np.linalg.norm(inter[r] - ref_i) / np.linalg.norm(ref_i)
+        assert err_i < 8e-3, f"inter row {r} (pair {p}, expert {e}): rel err {err_i:.3e}"
+        y = inter[r] @ orc.dequantize(wn["w2"][e], wn["w2_sf"][e], wn["w2_gs"][e]).T * (1 + pnw)
+        err_y = np.linalg.norm(ypart[r] - y) / np.linalg.norm(y)
+        assert err_y < 1e-4, f"ypart row {r}: rel err {err_y:.3e}"
+        assert abs(ssq[r] - float((y * y).sum())) <= 1e-3 * float((y * y).sum())
