@@ -5,7 +5,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
-#include "../../include/muse_moe.h"
+#include "muse_moe.h"
 
 namespace muse {
 

@@ -48,14 +48,17 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
-// Wait until the phase with parity `parity` has completed. Returns false on timeout.
+// Wait until the phase with parity `parity` has completed. Returns false after kWaitCycles
+// (the clock is read once per 64 polls).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 64; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
     if (clock64() - t0 > kWaitCycles) return false;
   }
-  return true;
 }
 
 // ----------------------------------------------------------------------------- copies
