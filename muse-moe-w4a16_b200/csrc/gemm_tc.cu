@@ -7,20 +7,21 @@
 //                   (fp32) and the per-pair sum of squares -> ssq (reference.py:88-90, 105)
 //
 // One persistent CTA per SM walks a static list of (expert, 128-row tile, token tile) items.
-// A tcgen05.mma costs its issuing thread ~44 cycles however small N is, so a CTA runs TWO
-// independent pipelines (even / odd items of its list), each with its own issuer:
+// A tcgen05.mma costs its issuing thread ~44 cycles however small N is (measured on B200), so
+// a CTA runs P independent pipelines (P = 3 for the 16-token decode tile, else 2); item j of
+// the CTA's list goes to pipeline j % P. Warp roles:
 //
-//   warps 0,1    producers (pipeline 0, 1): 1-D bulk copies of the prepared fp4 code and
-//                scale tiles, 2-D TMA boxes of the activations (128-byte swizzle)
-//   warps 2,3    MMA issuers (pipeline 0, 1): tcgen05.mma, A in tensor memory, B in shared
-//                memory, fp32 accumulators in tensor memory; warp 2 also owns the allocation
-//   warps 4-7    epilogue for both pipelines (items in list order): tcgen05.ld, fused
-//                activation / post-norm, stores
-//   warps 8-11   dequantisers of pipeline 0; warps 12-15 of pipeline 1. Thread = weight row:
-//                e2m1 x e4m3 -> exact bf16 in registers, tcgen05.st into an A buffer
+//   warps [0, P)        producers: 1-D bulk copies of the prepared fp4 code and scale tiles,
+//                       2-D TMA boxes of the activations (128-byte swizzle)
+//   warps [P, 2P)       MMA issuers: tcgen05.mma, A in tensor memory, B in shared memory,
+//                       fp32 accumulators in tensor memory; warp P also owns the allocation
+//   warps [2P, 2P+4)    epilogue for all pipelines (items in list order): tcgen05.ld, fused
+//                       activation / post-norm, stores
+//   4 warps per pipeline dequantisers. Thread = weight row: e2m1 x e4m3 -> exact bf16 in
+//                       registers, tcgen05.st into an A buffer
 //
-// Tensor memory: pipeline p owns columns [256p, 256p + 256): n_a A buffers of 64 columns
-// (128 K elements as bf16 pairs) followed by n_acc accumulators of n_box columns.
+// Tensor memory: pipeline p owns a column range of 512/P (rounded to 32): n_a A buffers of
+// 64 columns (128 K elements as bf16 pairs) followed by n_acc accumulators of n_box columns.
 // Every mbarrier wait is bounded; on timeout the CTA records an error flag and unwinds.
 #include "common.cuh"
 #include "kernels.cuh"
@@ -31,14 +32,18 @@ namespace muse {
 
 namespace {
 
-constexpr int kThreads = 512;
-constexpr int kPipes = 2;
-constexpr int kMmaWarp0 = 2;
-constexpr int kEpiWarp0 = 4;
-constexpr int kDeqWarp0 = 8;
+constexpr int kMaxPipes = 3;
 constexpr int kACols = kChunkK / 2;   // TMEM columns per A buffer (bf16 pairs)
-constexpr int kPipeCols = 256;
 constexpr int kTmemCols = 512;
+
+template <int P> struct Roles {
+  static constexpr int kMmaWarp0 = P;
+  static constexpr int kEpiWarp0 = 2 * P;
+  static constexpr int kDeqWarp0 = 2 * P + 4;
+  static constexpr int kWarps = 2 * P + 4 + 4 * P;
+  static constexpr int kThreads = 32 * kWarps;
+  static constexpr int kPipeCols = (kTmemCols / P) / 32 * 32;
+};
 constexpr int kMaxStages = 8;
 constexpr int kMaxABuf = 3;
 constexpr int kMaxExperts = kMaxLocalExperts;
@@ -56,7 +61,7 @@ struct PipeCtl {
 };
 
 struct SharedCtl {
-  PipeCtl pipe[kPipes];
+  PipeCtl pipe[kMaxPipes];
   uint32_t tmem_base;
   int total_items;
   int item_prefix[kMaxExperts + 1];  // cumulative items per expert
@@ -72,12 +77,12 @@ struct Geo {
   uint32_t b_bytes, stage_bytes;
 };
 
-__host__ __device__ inline Geo make_geo(int n_box, int stages) {
+__host__ __device__ inline Geo make_geo(int pipe_cols, int n_box, int stages) {
   Geo g;
   g.S = stages;
   g.n_box = n_box;
-  g.n_acc = 2 * n_box <= 128 ? 2 : 1;
-  g.n_a = (kPipeCols - g.n_acc * n_box) / kACols;
+  g.n_acc = 2 * n_box <= pipe_cols / 2 ? 2 : 1;
+  g.n_a = (pipe_cols - g.n_acc * n_box) / kACols;
   if (g.n_a > kMaxABuf) g.n_a = kMaxABuf;
   g.b_bytes = 2u * n_box * 128u;
   g.stage_bytes = g.b_bytes + kTileCodeBytes + kTileScaleBytes;
@@ -137,11 +142,16 @@ __device__ __forceinline__ void record_error(int* flag, int code) {
   if (flag) atomicExch(flag, code);
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+template <int P>
+__global__ void __launch_bounds__(Roles<P>::kThreads, 1)
 expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
+  using R = Roles<P>;
+  constexpr int kPipes = P;
+  constexpr int kMmaWarp0 = R::kMmaWarp0, kEpiWarp0 = R::kEpiWarp0, kDeqWarp0 = R::kDeqWarp0;
+  constexpr int kPipeCols = R::kPipeCols;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const Geo geo = make_geo(a.n_box, a.stages);
+  const Geo geo = make_geo(kPipeCols, a.n_box, a.stages);
   const int S = geo.S, n_box = geo.n_box;
   SharedCtl& ctl = *reinterpret_cast<SharedCtl*>(smem + (size_t)kPipes * S * geo.stage_bytes);
   // stage s of pipeline p: [B boxes | fp4 codes | scales]
@@ -261,30 +271,34 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
       const uint32_t idesc = ptx::idesc_bf16_f32(kTileM, n_box);
       const uint32_t col0 = tbase + p * kPipeCols;
       const uint32_t acc_col0 = col0 + geo.n_a * kACols;
+      // The dequantisers arrive on a_full only after observing the stage's full barrier, so
+      // a_full alone orders the MMAs after both the A buffer and the stage's B boxes.
       Ring st, ar, accr;
+      const uint64_t desc_first = ptx::smem_desc_k_sw128(ptx::smem_u32(stage_ptr(p, 0)), 1024);
+      const uint32_t stage_step = geo.stage_bytes >> 4;       // descriptor units (16 B)
+      const uint32_t atom_step = (uint32_t)(n_box * 128) >> 4;  // second 64-K box of a stage
+      uint64_t desc_stage = desc_first;
       for (int j = p; ok && blockIdx.x + j * G < total; j += kPipes, accr.next(geo.n_acc)) {
         const int acc = accr.slot;
         if (!ptx::mbar_wait(&pc.acc_empty[acc], accr.phase ^ 1)) { ok = false; break; }
         ptx::tc_fence_after();
         const uint32_t d_tmem = acc_col0 + acc * n_box;
-        for (int kc = 0; kc < a.k_chunks; ++kc, st.next(S), ar.next(geo.n_a)) {
+        for (int kc = 0; kc < a.k_chunks; ++kc) {
           const int s = st.slot;
           const int ab = ar.slot;
-          if (!ptx::mbar_wait(&pc.full[s], st.phase) || !ptx::mbar_wait(&pc.a_full[ab], ar.phase)) {
-            ok = false;
-            break;
-          }
+          if (!ptx::mbar_wait(&pc.a_full[ab], ar.phase)) { ok = false; break; }
           ptx::tc_fence_after();
-          const uint64_t bdesc0 = ptx::smem_desc_k_sw128(ptx::smem_u32(stage_ptr(p, s)), 1024);
           const uint32_t a_tmem = col0 + ab * kACols;
-          const uint64_t atom_step = (uint64_t)((n_box * 128) >> 4);  // second 64-K box
 #pragma unroll
           for (int kk = 0; kk < kChunkK / 16; ++kk) {
-            const uint64_t bdesc = bdesc0 + (kk >> 2) * atom_step + (uint64_t)((kk & 3) * 2);
+            const uint64_t bdesc = desc_stage + (uint64_t)((kk >> 2) * atom_step + (kk & 3) * 2);
             ptx::mma_bf16_ts(d_tmem, a_tmem + kk * 8, bdesc, idesc, (kc | kk) != 0);
           }
           ptx::mma_commit(&pc.empty[s]);
           ptx::mma_commit(&pc.a_empty[ab]);
+          ar.next(geo.n_a);
+          st.next(S);
+          desc_stage = st.slot == 0 ? desc_first : desc_stage + stage_step;
         }
         if (!ok) break;
         ptx::mma_commit(&pc.acc_full[acc]);
@@ -300,7 +314,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
     bool ok = true;
     Ring accr[kPipes];
     for (int j = 0; blockIdx.x + j * G < total; ++j) {
-      const int p = j & (kPipes - 1);
+      const int p = j % kPipes;
       PipeCtl& pc = ctl.pipe[p];
       const Item t = decode_item(ctl, a.offsets, blockIdx.x + j * G, n_local, n_box);
       const int acc = accr[p].slot;
@@ -410,6 +424,12 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
   if (warp == kMmaWarp0) ptx::tmem_dealloc(tbase, kTmemCols);
 }
 
+// Host-side view of one instantiation.
+template <int P> struct Variant {
+  static constexpr int kThreads = Roles<P>::kThreads;
+  static constexpr int kPipeCols = Roles<P>::kPipeCols;
+};
+
 int g_num_sms[64] = {0};
 bool g_attr_set[64] = {false};
 
@@ -433,15 +453,22 @@ int read_device_status(int* status, int reset) {
   return e;
 }
 
+// Pipelines per CTA for a token tile: three issuers fit the tensor memory only with N = 16.
+int pick_pipes(int n_box) { return n_box <= 16 ? 3 : 2; }
+
+int pipe_cols(int pipes) { return pipes == 3 ? Variant<3>::kPipeCols : Variant<2>::kPipeCols; }
+
 size_t gemm_smem_bytes(int n_box, int stages) {
-  const Geo g = make_geo(n_box, stages);
-  return 1024 + (size_t)kPipes * stages * g.stage_bytes + sizeof(SharedCtl);
+  const int P = pick_pipes(n_box);
+  const Geo g = make_geo(pipe_cols(P), n_box, stages);
+  return 1024 + (size_t)P * stages * g.stage_bytes + sizeof(SharedCtl);
 }
 
 int pick_stages(int n_box) {
-  const Geo g = make_geo(n_box, 1);
+  const int P = pick_pipes(n_box);
+  const Geo g = make_geo(pipe_cols(P), n_box, 1);
   const size_t budget = 220u * 1024u - sizeof(SharedCtl) - 1024;
-  int s = (int)(budget / (kPipes * g.stage_bytes));
+  int s = (int)(budget / (P * g.stage_bytes));
   return s < kMaxStages ? s : kMaxStages;
 }
 
@@ -455,13 +482,20 @@ int launch_expert_gemm(const CUtensorMap& tmap_b, const GemmArgs& args, cudaStre
     if (e != cudaSuccess) return e;
   }
   if (!g_attr_set[dev]) {
-    e = cudaFuncSetAttribute(expert_gemm_tc, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    e = cudaFuncSetAttribute(expert_gemm_tc<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e == cudaSuccess)
+      e = cudaFuncSetAttribute(expert_gemm_tc<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
     g_attr_set[dev] = true;
   }
   if (args.stages < 2) return MUSE_ERR_UNSUPPORTED_SHAPE;
+  const Geo g = make_geo(pipe_cols(pick_pipes(args.n_box)), args.n_box, args.stages);
+  if (g.n_a < 2) return MUSE_ERR_UNSUPPORTED_SHAPE;
   const size_t smem = gemm_smem_bytes(args.n_box, args.stages);
-  expert_gemm_tc<<<g_num_sms[dev], kThreads, smem, stream>>>(tmap_b, args);
+  if (pick_pipes(args.n_box) == 3)
+    expert_gemm_tc<3><<<g_num_sms[dev], Variant<3>::kThreads, smem, stream>>>(tmap_b, args);
+  else
+    expert_gemm_tc<2><<<g_num_sms[dev], Variant<2>::kThreads, smem, stream>>>(tmap_b, args);
   return last_launch_status();
 }
 
