@@ -216,6 +216,8 @@ extern "C" int muse_moe_forward(const void* x, const int32_t* topk_ids, const fl
   g1.ld_out = inter;
   g1.inter = s.inter;
   g1.error_flag = s.error_flag;
+  g1.mul16 = 16;
+  g1.mul64 = 64;
   if ((rc = launch_expert_gemm(tmap_x, g1, st))) return rc;
 
   GemmArgs g2 = g1;

@@ -8,8 +8,9 @@
 //
 // One persistent CTA per SM walks a static list of (expert, 128-row tile, token tile) items.
 // A tcgen05.mma costs its issuing thread ~44 cycles however small N is (measured on B200), so
-// a CTA runs P independent pipelines (P = 3 for the 16-token decode tile, else 2); item j of
-// the CTA's list goes to pipeline j % P. Warp roles:
+// a CTA runs P independent pipelines (P = 3 for the 16-token decode tile, else 2) that split
+// the K chunks of each tile between them (split-K, one partial accumulator per pipeline,
+// summed by the epilogue). Warp roles:
 //
 //   warps [0, P)        producers: 1-D bulk copies of the prepared fp4 code and scale tiles,
 //                       2-D TMA boxes of the activations (128-byte swizzle)
@@ -130,12 +131,17 @@ __device__ __forceinline__ uint32_t hmul2_bf16(uint32_t a, uint32_t b) {
 }
 
 // One permuted code word (8 elements) -> 4 bf16x2 of e2m1 * sf * 2^-66 (layout.cuh).
-__device__ __forceinline__ void dequant8(uint32_t w, uint32_t scale2, uint32_t* out) {
+// The integer logic pipe and the multiply pipe each run these ops at half rate, so the two
+// left shifts that never need wrapped bits (rotl 4, and the << 6 of the last pair) are done
+// as multiplies by m16 = 16 and m64 = 64 -- values the compiler cannot see, so they stay on
+// the multiply pipe -- leaving 5 logic ops and 2 funnel shifts per word on the logic pipe.
+__device__ __forceinline__ void dequant8(uint32_t w, uint32_t scale2, uint32_t m16, uint32_t m64,
+                                         uint32_t* out) {
   constexpr uint32_t kMask = 0x81C081C0u;
   out[0] = hmul2_bf16(w & kMask, scale2);
-  out[1] = hmul2_bf16(ptx::rotl(w, 4) & kMask, scale2);
+  out[1] = hmul2_bf16((w * m16) & kMask, scale2);
   out[2] = hmul2_bf16(ptx::rotl(w, 10) & kMask, scale2);
-  out[3] = hmul2_bf16(((w << 6) & 0x80C080C0u) | ((w >> 2) & 0x01000100u), scale2);
+  out[3] = hmul2_bf16(((w * m64) & 0x80C080C0u) | ((w >> 2) & 0x01000100u), scale2);
 }
 
 __device__ __forceinline__ void record_error(int* flag, int code) {
@@ -222,7 +228,12 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
   const uint32_t tbase = ctl.tmem_base;
   const int total = ctl.total_items;
   const int G = gridDim.x;
-  // j-th item of this CTA: it = blockIdx.x + j * G; pipeline j % 2, pipeline-local index j / 2.
+  const int kcn = a.k_chunks;
+  // Tile j of this CTA is item blockIdx.x + j * G. Its K chunks are split over the pipelines
+  // (split-K): pipeline p takes the chunks kc with (kc + j) % P == p, into its own accumulator;
+  // the epilogue sums the partial accumulators. Rotating the assignment with j balances the
+  // pipelines when P does not divide the chunk count.
+  auto first_chunk = [&](int p, int jm) { return (p - jm + kPipes) % kPipes; };
 
   if (warp < kMmaWarp0) {
     // ------------------------------------------------------------------ producers
@@ -233,10 +244,13 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
       int stage = 0;
       uint32_t phase = 0;
       int issued = 0;
-      for (int j = p; ok && blockIdx.x + j * G < total; j += kPipes) {
+      int jm = 0;
+      for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
+        const int kc0 = first_chunk(p, jm);
+        if (kc0 >= kcn) continue;
         const Item t = decode_item(ctl, a.offsets, blockIdx.x + j * G, n_local, n_box);
-        const size_t tile0 = ((size_t)t.e * a.m_tiles + t.m) * a.k_chunks;
-        for (int kc = 0; kc < a.k_chunks; ++kc) {
+        const size_t tile0 = ((size_t)t.e * a.m_tiles + t.m) * kcn;
+        for (int kc = kc0; kc < kcn; kc += kPipes) {
           if (!ptx::mbar_wait(&pc.empty[stage], phase ^ 1)) { ok = false; break; }
           uint8_t* sp = stage_ptr(p, stage);
           ptx::mbar_arrive_expect_tx(&pc.full[stage], geo.stage_bytes);
@@ -278,12 +292,15 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
       const uint32_t stage_step = geo.stage_bytes >> 4;       // descriptor units (16 B)
       const uint32_t atom_step = (uint32_t)(n_box * 128) >> 4;  // second 64-K box of a stage
       uint64_t desc_stage = desc_first;
-      for (int j = p; ok && blockIdx.x + j * G < total; j += kPipes, accr.next(geo.n_acc)) {
+      int jm = 0;
+      for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
+        const int kc0 = first_chunk(p, jm);
+        if (kc0 >= kcn) continue;
         const int acc = accr.slot;
         if (!ptx::mbar_wait(&pc.acc_empty[acc], accr.phase ^ 1)) { ok = false; break; }
         ptx::tc_fence_after();
         const uint32_t d_tmem = acc_col0 + acc * n_box;
-        for (int kc = 0; kc < a.k_chunks; ++kc) {
+        for (int kc = kc0; kc < kcn; kc += kPipes) {
           const int s = st.slot;
           const int ab = ar.slot;
           if (!ptx::mbar_wait(&pc.a_full[ab], ar.phase)) { ok = false; break; }
@@ -292,7 +309,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
 #pragma unroll
           for (int kk = 0; kk < kChunkK / 16; ++kk) {
             const uint64_t bdesc = desc_stage + (uint64_t)((kk >> 2) * atom_step + (kk & 3) * 2);
-            ptx::mma_bf16_ts(d_tmem, a_tmem + kk * 8, bdesc, idesc, (kc | kk) != 0);
+            ptx::mma_bf16_ts(d_tmem, a_tmem + kk * 8, bdesc, idesc, (kc != kc0) | (kk != 0));
           }
           ptx::mma_commit(&pc.empty[s]);
           ptx::mma_commit(&pc.a_empty[ab]);
@@ -302,6 +319,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
         }
         if (!ok) break;
         ptx::mma_commit(&pc.acc_full[acc]);
+        accr.next(geo.n_acc);
       }
       if (!ok) record_error(a.error_flag, 2);
       // all issued MMAs complete before tensor memory is released
@@ -311,28 +329,42 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
   } else if (warp < kDeqWarp0) {
     // ------------------------------------------------------------------ epilogue
     const int q = warp & 3;
+    const uint32_t lane_base = tbase + ((uint32_t)(32 * q) << 16) + geo.n_a * kACols;
     bool ok = true;
     Ring accr[kPipes];
-    for (int j = 0; blockIdx.x + j * G < total; ++j) {
-      const int p = j % kPipes;
-      PipeCtl& pc = ctl.pipe[p];
+    int jm = 0;
+    for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
       const Item t = decode_item(ctl, a.offsets, blockIdx.x + j * G, n_local, n_box);
-      const int acc = accr[p].slot;
-      const uint32_t acc_phase = accr[p].phase;
-      accr[p].next(geo.n_acc);
-      if (!ptx::mbar_wait(&pc.acc_full[acc], acc_phase)) { ok = false; break; }
+      // partial accumulators of the participating pipelines
+      uint32_t taddr[kPipes];
+      int used = 0;
+#pragma unroll
+      for (int p = 0; p < kPipes; ++p) {
+        if (first_chunk(p, jm) >= kcn) continue;
+        if (!ptx::mbar_wait(&ctl.pipe[p].acc_full[accr[p].slot], accr[p].phase)) ok = false;
+        taddr[used++] = lane_base + p * kPipeCols + accr[p].slot * n_box;
+      }
+      if (!ok) break;
       ptx::tc_fence_after();
-      const uint32_t taddr = tbase + ((uint32_t)(32 * q) << 16) + p * kPipeCols + geo.n_a * kACols + acc * n_box;
       const float gsc = a.gs[t.e] * kUnscale;
       if (a.mode == 1) {
         const int jj = 64 * t.m + 16 * q + (lane & 15);  // intermediate index of this lane
         for (int cb = 0; cb * 16 < t.nvalid; ++cb) {
+          float acc[16];
           uint32_t v[16];
-          ptx::tmem_ld16(taddr + cb * 16, v);
+          ptx::tmem_ld16(taddr[0] + cb * 16, v);
           ptx::tmem_wait_ld();
 #pragma unroll
+          for (int c = 0; c < 16; ++c) acc[c] = __uint_as_float(v[c]);
+          for (int u = 1; u < used; ++u) {
+            ptx::tmem_ld16(taddr[u] + cb * 16, v);
+            ptx::tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 16; ++c) acc[c] += __uint_as_float(v[c]);
+          }
+#pragma unroll
           for (int col = 0; col < 16; ++col) {
-            const float mine = __uint_as_float(v[col]) * gsc;
+            const float mine = acc[col] * gsc;
             const float other = __shfl_xor_sync(0xffffffffu, mine, 16);
             const int n = cb * 16 + col;
             if (lane < 16 && n < t.nvalid) {
@@ -346,14 +378,23 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
         const int h = kTileM * t.m + 32 * q + lane;  // output row of this lane
         const float wn = gsc * (1.0f + bf16_bits_to_float(a.post_norm_w[h]));
         for (int cb = 0; cb * 16 < t.nvalid; ++cb) {
+          float acc[16];
           uint32_t v[16];
-          ptx::tmem_ld16(taddr + cb * 16, v);
+          ptx::tmem_ld16(taddr[0] + cb * 16, v);
           ptx::tmem_wait_ld();
+#pragma unroll
+          for (int c = 0; c < 16; ++c) acc[c] = __uint_as_float(v[c]);
+          for (int u = 1; u < used; ++u) {
+            ptx::tmem_ld16(taddr[u] + cb * 16, v);
+            ptx::tmem_wait_ld();
+#pragma unroll
+            for (int c = 0; c < 16; ++c) acc[c] += __uint_as_float(v[c]);
+          }
 #pragma unroll
           for (int col = 0; col < 16; ++col) {
             const int n = cb * 16 + col;
             if (n < t.nvalid) {  // warp-uniform
-              const float y = __uint_as_float(v[col]) * wn;
+              const float y = acc[col] * wn;
               a.ypart[(size_t)(t.row0 + n) * a.ld_out + h] = y;
               float s2 = y * y;
 #pragma unroll
@@ -365,7 +406,12 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
       }
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&pc.acc_empty[acc]);
+#pragma unroll
+      for (int p = 0; p < kPipes; ++p) {
+        if (first_chunk(p, jm) >= kcn) continue;
+        if (lane == 0) ptx::mbar_arrive(&ctl.pipe[p].acc_empty[accr[p].slot]);
+        accr[p].next(geo.n_acc);
+      }
     }
     if (!ok && lane == 0) record_error(a.error_flag, 3);
   } else {
@@ -375,10 +421,12 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
     const int q = warp & 3;                  // TMEM lane quarter
     const int row = 32 * q + lane;           // weight row of this thread
     const uint32_t lane_col0 = tbase + ((uint32_t)(32 * q) << 16) + p * kPipeCols;
+    const uint32_t m16 = a.mul16, m64 = a.mul64;
     bool ok = true;
     Ring st, ar;
-    for (int j = p; ok && blockIdx.x + j * G < total; j += kPipes) {
-      for (int kc = 0; kc < a.k_chunks; ++kc, st.next(S), ar.next(geo.n_a)) {
+    int jm = 0;
+    for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
+      for (int kc = first_chunk(p, jm); kc < kcn; kc += kPipes, st.next(S), ar.next(geo.n_a)) {
         const int s = st.slot;
         const int ab = ar.slot;
         if (!ptx::mbar_wait(&pc.full[s], st.phase) || !ptx::mbar_wait(&pc.a_empty[ab], ar.phase ^ 1)) {
@@ -396,14 +444,14 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
           const uint32_t sc[4] = {ctl.scale_lut[sw & 0xFF], ctl.scale_lut[(sw >> 8) & 0xFF],
                                   ctl.scale_lut[(sw >> 16) & 0xFF], ctl.scale_lut[sw >> 24]};
           uint32_t out[32];
-          dequant8(c0.x, sc[0], &out[0]);
-          dequant8(c0.y, sc[0], &out[4]);
-          dequant8(c0.z, sc[1], &out[8]);
-          dequant8(c0.w, sc[1], &out[12]);
-          dequant8(c1.x, sc[2], &out[16]);
-          dequant8(c1.y, sc[2], &out[20]);
-          dequant8(c1.z, sc[3], &out[24]);
-          dequant8(c1.w, sc[3], &out[28]);
+          dequant8(c0.x, sc[0], m16, m64, &out[0]);
+          dequant8(c0.y, sc[0], m16, m64, &out[4]);
+          dequant8(c0.z, sc[1], m16, m64, &out[8]);
+          dequant8(c0.w, sc[1], m16, m64, &out[12]);
+          dequant8(c1.x, sc[2], m16, m64, &out[16]);
+          dequant8(c1.y, sc[2], m16, m64, &out[20]);
+          dequant8(c1.z, sc[3], m16, m64, &out[24]);
+          dequant8(c1.w, sc[3], m16, m64, &out[28]);
           ptx::tmem_st32(lane_col0 + ab * kACols + half * 32, out);
         }
         ptx::tmem_wait_st();

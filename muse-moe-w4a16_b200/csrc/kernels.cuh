@@ -55,6 +55,7 @@ struct GemmArgs {
   float* ypart;
   float* ssq;
   int* error_flag;
+  uint32_t mul16, mul64;   // 16 and 64, passed at run time (see dequant8 in gemm_tc.cu)
 };
 
 int launch_route(const int32_t* ids, int tokens, int top_k, int local_start, int local_count,
