@@ -251,7 +251,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
         const Item t = decode_item(ctl, a.offsets, blockIdx.x + j * G, n_local, n_box);
         const size_t tile0 = ((size_t)t.e * a.m_tiles + t.m) * kcn;
         for (int kc = kc0; kc < kcn; kc += kPipes) {
-          if (!ptx::mbar_wait(&pc.empty[stage], phase ^ 1)) { ok = false; break; }
+          if (!ptx::mbar_wait_sleep(&pc.empty[stage], phase ^ 1)) { ok = false; break; }
           uint8_t* sp = stage_ptr(p, stage);
           ptx::mbar_arrive_expect_tx(&pc.full[stage], geo.stage_bytes);
           ptx::bulk_g2s(sp + geo.b_bytes, a.wq + (tile0 + kc) * kTileCodeBytes, kTileCodeBytes, &pc.full[stage]);
@@ -297,7 +297,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
         const int kc0 = first_chunk(p, jm);
         if (kc0 >= kcn) continue;
         const int acc = accr.slot;
-        if (!ptx::mbar_wait(&pc.acc_empty[acc], accr.phase ^ 1)) { ok = false; break; }
+        if (!ptx::mbar_wait_sleep(&pc.acc_empty[acc], accr.phase ^ 1)) { ok = false; break; }
         ptx::tc_fence_after();
         const uint32_t d_tmem = acc_col0 + acc * n_box;
         for (int kc = kc0; kc < kcn; kc += kPipes) {
@@ -341,7 +341,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
 #pragma unroll
       for (int p = 0; p < kPipes; ++p) {
         if (first_chunk(p, jm) >= kcn) continue;
-        if (!ptx::mbar_wait(&ctl.pipe[p].acc_full[accr[p].slot], accr[p].phase)) ok = false;
+        if (!ptx::mbar_wait_sleep(&ctl.pipe[p].acc_full[accr[p].slot], accr[p].phase)) ok = false;
         taddr[used++] = lane_base + p * kPipeCols + accr[p].slot * n_box;
       }
       if (!ok) break;
@@ -441,8 +441,10 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
           const uint4 c0 = *reinterpret_cast<const uint4*>(arow + 16 * code_slot(row, 2 * half));
           const uint4 c1 = *reinterpret_cast<const uint4*>(arow + 16 * code_slot(row, 2 * half + 1));
           const uint32_t sw = half ? sfw.y : sfw.x;  // the 4 scale bytes of these 64 elements
-          const uint32_t sc[4] = {ctl.scale_lut[sw & 0xFF], ctl.scale_lut[(sw >> 8) & 0xFF],
-                                  ctl.scale_lut[(sw >> 16) & 0xFF], ctl.scale_lut[sw >> 24]};
+          const uint32_t sc[4] = {ctl.scale_lut[__byte_perm(sw, 0, 0x4440)],
+                                  ctl.scale_lut[__byte_perm(sw, 0, 0x4441)],
+                                  ctl.scale_lut[__byte_perm(sw, 0, 0x4442)],
+                                  ctl.scale_lut[__byte_perm(sw, 0, 0x4443)]};
           uint32_t out[32];
           dequant8(c0.x, sc[0], m16, m64, &out[0]);
           dequant8(c0.y, sc[0], m16, m64, &out[4]);

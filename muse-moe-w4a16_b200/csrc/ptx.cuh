@@ -48,8 +48,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return done != 0;
 }
 
+// As mbar_try_wait, but an incomplete phase suspends the thread in hardware for up to
+// `hint_ns` nanoseconds (it wakes early when the phase completes), so it issues nothing.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t done;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(done)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return done != 0;
+}
+
 // Wait until the phase with parity `parity` has completed. Returns false after kWaitCycles
-// (the clock is read once per 64 polls).
+// (the clock is read once per 64 polls). Used by the roles on the critical path.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
@@ -57,6 +71,17 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 #pragma unroll 1
     for (int i = 0; i < 64; ++i)
       if (mbar_try_wait(bar, parity)) return true;
+    if (clock64() - t0 > kWaitCycles) return false;
+  }
+}
+
+// The same bound, for roles that may wait a long time (a whole tile): the waiting thread
+// sleeps in the barrier instead of polling, leaving the issue slots to the other warps.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 20000)) return true;
     if (clock64() - t0 > kWaitCycles) return false;
   }
 }
