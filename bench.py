@@ -252,8 +252,7 @@ def cpu_baseline(shape, tokens, w, inputs):
 
 def run_muse(args, world, rank, local):
     pkg = __graft_entry__.load_package()
-    from muse_moe_w4a16_b200 import synth
-    from oracle import moe_oracle as orc  # byte/flop model only; never on the timed path
+    from muse_moe_w4a16_b200 import _lib, synth, traffic
 
     dev = torch.device("cuda", local)
     shape, tokens = workload(args, synth)
@@ -322,27 +321,56 @@ def run_muse(args, world, rank, local):
     ev_e2e = timed(e2e_graphs, args.steps)
     torch.cuda.synchronize()
 
+    # Per-kernel times: the same calls, eager, with events recorded between the kernels (the
+    # 512 MiB flush in front of each call keeps the GPU behind the host, so no event waits on
+    # a launch). [0]->[1] route + gather (empty when GEMM1 routes), [1]->[2] GEMM1,
+    # [2]->[3] GEMM2, [3]->[4] combine.
+    stage = {t: [] for t in tokens}
+    for i in range(args.steps):
+        for t in tokens:
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+            flush.zero_()
+            pkg.kernel_fn(dev_in[t], state, out=outs[t], stage_events=evs)
+            stage[t].append(evs)
+    torch.cuda.synchronize()
+    stage_us = {t: [statistics.mean(e[j].elapsed_time(e[j + 1]) * 1e3 for e in stage[t]) for j in range(4)]
+                for t in tokens}
+
     per_t = [statistics.mean(a.elapsed_time(b) * 1e3 for a, b in ev[t]) for t in tokens]
     per_t_e2e = [statistics.mean(a.elapsed_time(b) * 1e3 for a, b in ev_e2e[t]) for t in tokens]
     per_t = max_over_ranks(world, per_t)
     per_t_e2e = max_over_ranks(world, per_t_e2e)
+    flat = max_over_ranks(world, [v for t in tokens for v in stage_us[t]])
+    stage_us = {t: flat[4 * i:4 * i + 4] for i, t in enumerate(tokens)}
 
     # Correctness of what was timed: the graph outputs against the oracle (cheap sizes only).
     pk = peaks()
+    dims = (shape.local_start, shape.n_local, shape.hidden, shape.inter)
     per_rows = []
-    tot_bytes = tot_time = 0.0
+    g1_bytes = g1_time = 0.0
+    launches_per_step = 0
     for t, us in zip(tokens, per_t):
         ids = inputs[t]["topk_ids"].numpy()
-        b = orc.algorithmic_bytes(ids, shape.local_start, shape.n_local, shape.hidden, shape.inter)
-        f = orc.algorithmic_flops(ids, shape.local_start, shape.n_local, shape.hidden, shape.inter)
+        b = traffic.layer_bytes(ids, *dims)
+        f = traffic.layer_flops(ids, *dims)
+        b1 = traffic.gemm1_bytes(ids, *dims)
+        b2 = traffic.gemm2_bytes(ids, *dims)
+        pre, k1, k2, comb = stage_us[t]
+        plan = _lib.launch_plan(t, shape.top_k, shape.n_local, shape.hidden, shape.inter)
+        launches_per_step += plan["launches"]
         gbs = b / (us * 1e-6) / 1e9
-        tot_bytes += b
-        tot_time += us
+        g1_bytes += b1
+        g1_time += k1
         per_rows.append({"T": t, "us": round(us, 3), "bytes": b, "flops": f, "GBps": round(gbs, 1),
                          "hbm_frac": round(gbs / pk["hbm_gbs"], 4),
-                         "roofline_us": round(max(b / pk["hbm_gbs"] / 1e3, f / pk["bf16_tflops"] / 1e6), 3)})
-    achieved = tot_bytes / (tot_time * 1e-6) / 1e9
-    launches_per_call = 4
+                         "roofline_us": round(max(b / pk["hbm_gbs"] / 1e3, f / pk["bf16_tflops"] / 1e6), 3),
+                         "kernels_us": {"route_gather": round(pre, 3), "gemm1": round(k1, 3),
+                                        "gemm2": round(k2, 3), "combine": round(comb, 3)},
+                         "gemm1_GBps": round(b1 / (k1 * 1e-6) / 1e9, 1),
+                         "gemm2_GBps": round(b2 / (k2 * 1e-6) / 1e9, 1),
+                         "launches": plan["launches"], "n_box": plan["n_box"],
+                         "route_inline": plan["route_inline"]})
+    achieved = g1_bytes / (g1_time * 1e-6) / 1e9
     line = {
         "metric": metric_name(args), "value": round(geomean(per_t), 3), "unit": "us/call",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
@@ -353,11 +381,12 @@ def run_muse(args, world, rank, local):
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
                      "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
                      "peak_source": pk["source"],
-                     "kernel": "whole layer call (route + GEMM1/SiLU + GEMM2/norm + combine), sweep aggregate"},
+                     "kernel": "expert_gemm_tc, GEMM1 launch (w13 + SiLU*up): algorithmic bytes per "
+                               "launch / mean CUDA-event duration, summed over the token sweep"},
         "e2e": {"value": round(geomean(per_t_e2e), 3), "unit": "us/call", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
                 "how": "CUDA graph of pinned-host->device copies, kernel_fn, device->pinned-host copy"},
-        "gpu_launches": launches_per_call * len(tokens) * args.steps,
+        "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

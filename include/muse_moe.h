@@ -59,7 +59,8 @@ int muse_moe_workspace_size(int tokens, int top_k, int local_count, int hidden, 
 /*
  * Byte offsets of the scratch buffers inside the workspace, for inspection by tests:
  * offsets[0..7] = expert_offsets, pair_order, pair_row, xs (bf16 [T*K, H] gathered hidden
- * states), inter (bf16 [T*K, I]), ypart (fp32 [T*K, H]), ssq (fp32 [T*K]), total bytes.
+ * states), inter (bf16 [T*K, I]), ypart (fp32 [T*K, H]), ssq (fp32 [T*K, H/32]: the sum of
+ * squares of each 32-column slice of a ypart row), total bytes.
  * Rows of xs / inter / ypart / ssq are in pair_order order.
  */
 int muse_moe_workspace_offsets(int tokens, int top_k, int local_count, int hidden, int inter,
@@ -114,6 +115,32 @@ int muse_moe_forward(const void* x, const int32_t* topk_ids, const float* topk_w
                      const uint8_t* w2p, const uint8_t* w2_sfp, const float* w2_gs,
                      const void* post_norm_w, void* out,
                      void* workspace, size_t workspace_bytes, muse_stream_t stream);
+
+/*
+ * muse_moe_forward, with five caller-created CUDA events (cudaEvent_t, passed as void*)
+ * recorded on `stream` around the kernels: [0] start, [1] before GEMM1, [2] after GEMM1,
+ * [3] after GEMM2, [4] after the combine. For per-kernel timing; same results as
+ * muse_moe_forward. No counterpart in the reference (which times whole kernel_fn calls);
+ * it replaces nothing.
+ */
+int muse_moe_forward_profiled(const void* x, const int32_t* topk_ids, const float* topk_weights,
+                              int tokens, int top_k, int local_start, int local_count,
+                              int hidden, int inter,
+                              const uint8_t* w13p, const uint8_t* w13_sfp, const float* w13_gs,
+                              const uint8_t* w2p, const uint8_t* w2_sfp, const float* w2_gs,
+                              const void* post_norm_w, void* out,
+                              void* workspace, size_t workspace_bytes, muse_stream_t stream,
+                              void* const* stage_events);
+
+/*
+ * The launch plan of one muse_moe_forward call for these shapes (host only, no device work):
+ *   plan[0] kernels launched (3 when the first GEMM routes in its prologue, else 5; 0 if T = 0)
+ *   plan[1] token tile (the MMA's N), plan[2] pipeline stages,
+ *   plan[3] 1 when routing and the activation gather run inside the first GEMM.
+ * No counterpart in the reference; a diagnostic for benchmarks and tests.
+ */
+int muse_moe_launch_plan(int tokens, int top_k, int local_count, int hidden, int inter,
+                         int* plan);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -26,6 +26,10 @@ SIGNATURES: dict[str, tuple] = {
     "muse_moe_route": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P]),
     "muse_moe_forward": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I,
                               _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P]),
+    "muse_moe_forward_profiled": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I,
+                                       _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P,
+                                       ctypes.POINTER(_P)]),
+    "muse_moe_launch_plan": (_I, [_I, _I, _I, _I, _I, ctypes.POINTER(_I)]),
 }
 
 # Return codes (include/muse_moe.h).
@@ -105,3 +109,10 @@ def workspace_size(tokens: int, top_k: int, local_count: int, hidden: int, inter
     n = ctypes.c_size_t(0)
     call("muse_moe_workspace_size", tokens, top_k, local_count, hidden, inter, ctypes.byref(n))
     return int(n.value)
+
+
+def launch_plan(tokens: int, top_k: int, local_count: int, hidden: int, inter: int) -> dict:
+    """Kernels, token tile, stages and routing mode of one forward call (include/muse_moe.h)."""
+    arr = (ctypes.c_int * 4)()
+    call("muse_moe_launch_plan", tokens, top_k, local_count, hidden, inter, arr)
+    return {"launches": arr[0], "n_box": arr[1], "stages": arr[2], "route_inline": bool(arr[3])}

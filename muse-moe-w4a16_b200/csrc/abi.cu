@@ -39,7 +39,7 @@ WorkspaceLayout workspace_layout(int tokens, int top_k, int local_count, int hid
   l.xs = take(2 * P * hidden);
   l.inter = take(2 * P * inter);
   l.ypart = take(4 * P * hidden);
-  l.ssq = take(4 * P);
+  l.ssq = take(4 * P * (hidden / 32));
   l.total = at;
   return l;
 }
@@ -151,13 +151,16 @@ extern "C" int muse_moe_prepare_weights(const uint8_t* w13, const uint8_t* w13_s
   return launch_prepare_tiles(w2, w2_sf, n_experts, hidden, inter, 0, w2_out, w2_sf_out, s);
 }
 
-extern "C" int muse_moe_forward(const void* x, const int32_t* topk_ids, const float* topk_weights,
-                                int tokens, int top_k, int local_start, int local_count,
-                                int hidden, int inter, const uint8_t* w13p,
-                                const uint8_t* w13_sfp, const float* w13_gs, const uint8_t* w2p,
-                                const uint8_t* w2_sfp, const float* w2_gs,
-                                const void* post_norm_w, void* out, void* workspace,
-                                size_t workspace_bytes, muse_stream_t stream) {
+namespace {
+
+// The launch sequence of one layer call. `ev` (optional) receives five event records on the
+// stream: start, before GEMM1, after GEMM1, after GEMM2, after the combine.
+int forward_impl(const void* x, const int32_t* topk_ids, const float* topk_weights, int tokens,
+                 int top_k, int local_start, int local_count, int hidden, int inter,
+                 const uint8_t* w13p, const uint8_t* w13_sfp, const float* w13_gs,
+                 const uint8_t* w2p, const uint8_t* w2_sfp, const float* w2_gs,
+                 const void* post_norm_w, void* out, void* workspace, size_t workspace_bytes,
+                 cudaStream_t st, cudaEvent_t* ev) {
   int rc = check_dims(tokens, top_k, local_start, local_count, hidden, inter);
   if (rc) return rc;
   if (tokens == 0) return MUSE_OK;
@@ -187,20 +190,26 @@ extern "C" int muse_moe_forward(const void* x, const int32_t* topk_ids, const fl
   const int rows = (int)pair_rows(tokens, top_k);
   const int n_box = pick_n_box(tokens, top_k, local_count);
   const int stages = pick_stages(n_box);
-  cudaStream_t st = (cudaStream_t)stream;
+  auto mark = [&](int i) -> int { return ev ? (int)cudaEventRecord(ev[i], st) : 0; };
 
-  CUtensorMap tmap_x, tmap_i;
-  if ((rc = make_bf16_tmap(&tmap_x, s.xs, rows, hidden, n_box))) return rc;
+  // Small batches: the first GEMM routes in its prologue and gathers x rows itself, so neither
+  // the route nor the gather kernel runs (and xs stays unused).
+  const bool inline_route = P <= kMaxInlinePairs && n_box <= kMaxInlineBox;
+
+  CUtensorMap tmap_xs, tmap_x, tmap_i;
+  if ((rc = make_bf16_tmap(&tmap_xs, s.xs, rows, hidden, n_box))) return rc;
+  if ((rc = make_bf16_tmap(&tmap_x, x, tokens, hidden, 1))) return rc;
   if ((rc = make_bf16_tmap(&tmap_i, s.inter, rows, inter, n_box))) return rc;
 
-  cudaError_t ce = cudaMemsetAsync(s.ssq, 0, sizeof(float) * P, st);
-  if (ce != cudaSuccess) return ce;
-  if ((rc = launch_route(topk_ids, tokens, top_k, local_start, local_count, s.offsets, s.pair_order,
-                         s.pair_row, st)))
-    return rc;
-  if ((rc = launch_gather(static_cast<const uint16_t*>(x), s.offsets, s.pair_order, local_count,
-                          top_k, P, hidden, s.xs, st)))
-    return rc;
+  if ((rc = mark(0))) return rc;
+  if (!inline_route) {
+    if ((rc = launch_route(topk_ids, tokens, top_k, local_start, local_count, s.offsets,
+                           s.pair_order, s.pair_row, st)))
+      return rc;
+    if ((rc = launch_gather(static_cast<const uint16_t*>(x), s.offsets, s.pair_order, local_count,
+                            top_k, P, hidden, s.xs, st)))
+      return rc;
+  }
 
   GemmArgs g1{};
   g1.offsets = s.offsets;
@@ -218,7 +227,16 @@ extern "C" int muse_moe_forward(const void* x, const int32_t* topk_ids, const fl
   g1.error_flag = s.error_flag;
   g1.mul16 = 16;
   g1.mul64 = 64;
-  if ((rc = launch_expert_gemm(tmap_x, g1, st))) return rc;
+  g1.route_inline = inline_route;
+  g1.ids = topk_ids;
+  g1.n_pairs = P;
+  g1.local_start = local_start;
+  g1.top_k = top_k;
+  g1.pair_order = s.pair_order;
+  g1.pair_row = s.pair_row;
+  if ((rc = mark(1))) return rc;
+  if ((rc = launch_expert_gemm(tmap_xs, tmap_x, g1, st))) return rc;
+  if ((rc = mark(2))) return rc;
 
   GemmArgs g2 = g1;
   g2.m_tiles = hidden / kTileM;
@@ -232,7 +250,57 @@ extern "C" int muse_moe_forward(const void* x, const int32_t* topk_ids, const fl
   g2.post_norm_w = static_cast<const uint16_t*>(post_norm_w);
   g2.ypart = s.ypart;
   g2.ssq = s.ssq;
-  if ((rc = launch_expert_gemm(tmap_i, g2, st))) return rc;
+  g2.route_inline = 0;
+  if ((rc = launch_expert_gemm(tmap_i, tmap_i, g2, st))) return rc;
+  if ((rc = mark(3))) return rc;
+  if ((rc = launch_combine(d, topk_ids, topk_weights, s, static_cast<uint16_t*>(out), st))) return rc;
+  return mark(4);
+}
 
-  return launch_combine(d, topk_ids, topk_weights, s, static_cast<uint16_t*>(out), st);
+}  // namespace
+
+extern "C" int muse_moe_forward(const void* x, const int32_t* topk_ids, const float* topk_weights,
+                                int tokens, int top_k, int local_start, int local_count,
+                                int hidden, int inter, const uint8_t* w13p,
+                                const uint8_t* w13_sfp, const float* w13_gs, const uint8_t* w2p,
+                                const uint8_t* w2_sfp, const float* w2_gs,
+                                const void* post_norm_w, void* out, void* workspace,
+                                size_t workspace_bytes, muse_stream_t stream) {
+  return forward_impl(x, topk_ids, topk_weights, tokens, top_k, local_start, local_count, hidden,
+                      inter, w13p, w13_sfp, w13_gs, w2p, w2_sfp, w2_gs, post_norm_w, out, workspace,
+                      workspace_bytes, (cudaStream_t)stream, nullptr);
+}
+
+extern "C" int muse_moe_forward_profiled(const void* x, const int32_t* topk_ids,
+                                         const float* topk_weights, int tokens, int top_k,
+                                         int local_start, int local_count, int hidden, int inter,
+                                         const uint8_t* w13p, const uint8_t* w13_sfp,
+                                         const float* w13_gs, const uint8_t* w2p,
+                                         const uint8_t* w2_sfp, const float* w2_gs,
+                                         const void* post_norm_w, void* out, void* workspace,
+                                         size_t workspace_bytes, muse_stream_t stream,
+                                         void* const* stage_events) {
+  if (!stage_events) return MUSE_ERR_INVALID_ARGUMENT;
+  cudaEvent_t ev[5];
+  for (int i = 0; i < 5; ++i) {
+    if (!stage_events[i]) return MUSE_ERR_INVALID_ARGUMENT;
+    ev[i] = static_cast<cudaEvent_t>(stage_events[i]);
+  }
+  return forward_impl(x, topk_ids, topk_weights, tokens, top_k, local_start, local_count, hidden,
+                      inter, w13p, w13_sfp, w13_gs, w2p, w2_sfp, w2_gs, post_norm_w, out, workspace,
+                      workspace_bytes, (cudaStream_t)stream, ev);
+}
+
+extern "C" int muse_moe_launch_plan(int tokens, int top_k, int local_count, int hidden, int inter,
+                                    int* plan) {
+  if (!plan) return MUSE_ERR_INVALID_ARGUMENT;
+  const int rc = check_dims(tokens, top_k, 0, local_count, hidden, inter);
+  if (rc) return rc;
+  const int n_box = pick_n_box(tokens, top_k, local_count);
+  const bool inline_route = tokens * top_k <= kMaxInlinePairs && n_box <= kMaxInlineBox;
+  plan[0] = tokens == 0 ? 0 : (inline_route ? 3 : 5);
+  plan[1] = n_box;
+  plan[2] = pick_stages(n_box);
+  plan[3] = inline_route ? 1 : 0;
+  return MUSE_OK;
 }

@@ -3,6 +3,8 @@
 // in fp32, cast to bf16 (reference.py:88-90, 106-107; the role of SGLang's Triton
 // fused_post_expert_norm_weighted_sum, baseline.py:149-151). Tokens with no local pair get
 // zeros. Slots are summed in ascending expert order, the order ref_kernel's index_add_ uses.
+// The sum of squares of a pair is added up from its H/32 slice sums in a fixed order, so the
+// result does not depend on how the GEMM's CTAs were scheduled.
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -13,7 +15,7 @@ namespace {
 constexpr int kThreads = 128;
 constexpr int kColsPerCta = kThreads * 4;
 
-// grid (tokens, ceil(H / 512)); the K slots of a token are read by K threads in parallel.
+// grid (tokens, ceil(H / 512)). Warp w reduces the slice sums of slots w, w + 4, ...
 __global__ void __launch_bounds__(kThreads)
 combine_kernel(const int32_t* __restrict__ ids, const float* __restrict__ topk_weights,
                const int32_t* __restrict__ pair_row, const float* __restrict__ ypart,
@@ -23,12 +25,22 @@ combine_kernel(const int32_t* __restrict__ ids, const float* __restrict__ topk_w
   __shared__ int s_order[kMaxTopK];
   __shared__ int s_n;
   const int t = blockIdx.x;
-  const int tid = threadIdx.x;
-  if (tid < top_k) {
-    const int p = pair_row[t * top_k + tid];
-    s_row[tid] = p;
-    s_key[tid] = ids[t * top_k + tid];
-    s_coef[tid] = p >= 0 ? topk_weights[t * top_k + tid] * rsqrtf(ssq[p] / (float)H + kPostNormEps) : 0.f;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int parts = H >> 5;
+  for (int s = warp; s < top_k; s += kThreads / 32) {
+    const int p = pair_row[t * top_k + s];
+    float sum = 0.f;
+    if (p >= 0) {
+      const float* src = ssq + (size_t)p * parts;
+      for (int j = lane; j < parts; j += 32) sum += src[j];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    }
+    if (lane == 0) {
+      s_row[s] = p;
+      s_key[s] = ids[t * top_k + s];
+      s_coef[s] = p >= 0 ? topk_weights[t * top_k + s] * rsqrtf(sum / (float)H + kPostNormEps) : 0.f;
+    }
   }
   __syncthreads();
   if (tid == 0) {

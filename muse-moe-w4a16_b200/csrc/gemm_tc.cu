@@ -4,7 +4,9 @@
 //   GEMM1 (mode 1): h = xs . W13^T over K = H, epilogue silu(gate) * up -> inter (bf16)
 //                   (reference.py:103-104; SGLang keeps inter in bf16, baseline.py:132)
 //   GEMM2 (mode 2): y = inter . W2^T over K = I, epilogue y * gs * (1 + post_norm_w) -> ypart
-//                   (fp32) and the per-pair sum of squares -> ssq (reference.py:88-90, 105)
+//                   (fp32) and, per pair, the sum of squares of each 32-row slice -> ssq
+//                   (reference.py:88-90, 105); every value is written exactly once, in a fixed
+//                   order, so the layer's output is bit-reproducible
 //
 // One persistent CTA per SM walks a static list of (expert, 128-row tile, token tile) items.
 // A tcgen05.mma costs its issuing thread ~44 cycles however small N is (measured on B200), so
@@ -28,6 +30,7 @@
 #include "kernels.cuh"
 #include "layout.cuh"
 #include "ptx.cuh"
+#include "route.cuh"
 
 namespace muse {
 
@@ -68,6 +71,8 @@ struct SharedCtl {
   int item_prefix[kMaxExperts + 1];  // cumulative items per expert
   int ntiles[kMaxExperts];           // token tiles per expert
   uint32_t scale_lut[256];           // e4m3 byte -> bf16x2 (sf * 2^60, sf * 2^60)
+  int offs[kMaxExperts + 1];         // route_inline: expert ranges of the pair rows
+  int order[kMaxInlinePairs];        // route_inline: token of each expert-grouped pair row
 };
 
 // Per-launch geometry shared by all roles.
@@ -150,7 +155,8 @@ __device__ __forceinline__ void record_error(int* flag, int code) {
 
 template <int P>
 __global__ void __launch_bounds__(Roles<P>::kThreads, 1)
-expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
+expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_x,
+               const GemmArgs a) {
   using R = Roles<P>;
   constexpr int kPipes = P;
   constexpr int kMmaWarp0 = R::kMmaWarp0, kEpiWarp0 = R::kEpiWarp0, kDeqWarp0 = R::kDeqWarp0;
@@ -186,7 +192,19 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
     }
     ptx::fence_barrier_init();
   }
-  if (warp < kPipes && lane == 0) ptx::prefetch_tensormap(&tmap_b);
+  if (warp < kPipes && lane == 0) ptx::prefetch_tensormap(a.route_inline ? &tmap_x : &tmap_b);
+  // Expert ranges: from the route kernel, or (small batches) computed here by every CTA, with
+  // the stage buffers as scratch -- nothing is copied into them before the prologue ends.
+  const int32_t* offs = a.offsets;
+  if (a.route_inline) {
+    route_block(a.ids, a.n_pairs, a.local_start, n_local, reinterpret_cast<int*>(smem), ctl.offs,
+                ctl.order, blockIdx.x == 0 ? a.pair_row : nullptr);
+    if (blockIdx.x == 0) {
+      for (int i = threadIdx.x; i <= n_local; i += R::kThreads) a.offsets[i] = ctl.offs[i];
+      for (int i = threadIdx.x; i < a.n_pairs; i += R::kThreads) a.pair_order[i] = ctl.order[i];
+    }
+    offs = ctl.offs;
+  }
   if (threadIdx.x < 256) {
     const float f = e4m3_to_float(threadIdx.x) * 1152921504606846976.0f;  // * 2^60
     const __nv_bfloat16 h = __float2bfloat16_rn(f);
@@ -195,7 +213,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
     // items per expert, warp-inclusive scan (completed across warps below)
     const int e = threadIdx.x;
     int cnt = 0;
-    if (e < n_local) cnt = a.offsets[e + 1] - a.offsets[e];
+    if (e < n_local) cnt = offs[e + 1] - offs[e];
     const int nt = (cnt + n_box - 1) / n_box;
     if (e < n_local) ctl.ntiles[e] = nt;
     int incl = nt * a.m_tiles;
@@ -213,6 +231,10 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
+  if (a.route_inline) {  // pair index -> token (CTA 0 has published the pair indices above)
+    for (int i = threadIdx.x; i < a.n_pairs; i += R::kThreads)
+      if (ctl.order[i] >= 0) ctl.order[i] /= a.top_k;
+  }
   if (threadIdx.x == 0) {
     ctl.item_prefix[0] = 0;
     int carry = 0;
@@ -248,17 +270,34 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
       for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
         const int kc0 = first_chunk(p, jm);
         if (kc0 >= kcn) continue;
-        const Item t = decode_item(ctl, a.offsets, blockIdx.x + j * G, n_local, n_box);
+        const Item t = decode_item(ctl, offs, blockIdx.x + j * G, n_local, n_box);
         const size_t tile0 = ((size_t)t.e * a.m_tiles + t.m) * kcn;
         for (int kc = kc0; kc < kcn; kc += kPipes) {
           if (!ptx::mbar_wait_sleep(&pc.empty[stage], phase ^ 1)) { ok = false; break; }
           uint8_t* sp = stage_ptr(p, stage);
-          ptx::mbar_arrive_expect_tx(&pc.full[stage], geo.stage_bytes);
+          if (a.route_inline) {
+            // Activation rows straight from x[token], four rows per gather; only the groups that
+            // hold the tile's pairs are loaded (the MMA columns of the rest are never read).
+            const int groups = (t.nvalid + 3) >> 2;
+            ptx::mbar_arrive_expect_tx(&pc.full[stage], kTileCodeBytes + kTileScaleBytes + groups * 1024);
+            const int* tok = ctl.order + t.row0;
+            const int last = t.nvalid - 1;
+            for (int g4 = 0; g4 < groups; ++g4) {
+              const int i = 4 * g4;
+              const int r0 = tok[i], r1 = tok[min(i + 1, last)], r2 = tok[min(i + 2, last)],
+                        r3 = tok[min(i + 3, last)];
+              ptx::tma_gather4_2d(sp + i * 128, &tmap_x, kc * kChunkK, r0, r1, r2, r3, &pc.full[stage]);
+              ptx::tma_gather4_2d(sp + (n_box + i) * 128, &tmap_x, kc * kChunkK + 64, r0, r1, r2, r3,
+                                  &pc.full[stage]);
+            }
+          } else {
+            ptx::mbar_arrive_expect_tx(&pc.full[stage], geo.stage_bytes);
+            ptx::tma_load_2d(sp, &tmap_b, kc * kChunkK, t.row0, &pc.full[stage]);
+            ptx::tma_load_2d(sp + n_box * 128, &tmap_b, kc * kChunkK + 64, t.row0, &pc.full[stage]);
+          }
           ptx::bulk_g2s(sp + geo.b_bytes, a.wq + (tile0 + kc) * kTileCodeBytes, kTileCodeBytes, &pc.full[stage]);
           ptx::bulk_g2s(sp + geo.b_bytes + kTileCodeBytes, a.wsf + (tile0 + kc) * kTileScaleBytes,
                         kTileScaleBytes, &pc.full[stage]);
-          ptx::tma_load_2d(sp, &tmap_b, kc * kChunkK, t.row0, &pc.full[stage]);
-          ptx::tma_load_2d(sp + n_box * 128, &tmap_b, kc * kChunkK + 64, t.row0, &pc.full[stage]);
           ++issued;
           if (++stage == S) { stage = 0; phase ^= 1; }
         }
@@ -334,7 +373,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
     Ring accr[kPipes];
     int jm = 0;
     for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
-      const Item t = decode_item(ctl, a.offsets, blockIdx.x + j * G, n_local, n_box);
+      const Item t = decode_item(ctl, offs, blockIdx.x + j * G, n_local, n_box);
       // partial accumulators of the participating pipelines
       uint32_t taddr[kPipes];
       int used = 0;
@@ -399,7 +438,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const GemmArgs a) {
               float s2 = y * y;
 #pragma unroll
               for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-              if (lane == 0) atomicAdd(&a.ssq[t.row0 + n], s2);
+              if (lane == 0) a.ssq[(size_t)(t.row0 + n) * (a.ld_out >> 5) + (h >> 5)] = s2;
             }
           }
         }
@@ -522,7 +561,8 @@ int pick_stages(int n_box) {
   return s < kMaxStages ? s : kMaxStages;
 }
 
-int launch_expert_gemm(const CUtensorMap& tmap_b, const GemmArgs& args, cudaStream_t stream) {
+int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, const GemmArgs& args,
+                       cudaStream_t stream) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -541,11 +581,15 @@ int launch_expert_gemm(const CUtensorMap& tmap_b, const GemmArgs& args, cudaStre
   if (args.stages < 2) return MUSE_ERR_UNSUPPORTED_SHAPE;
   const Geo g = make_geo(pipe_cols(pick_pipes(args.n_box)), args.n_box, args.stages);
   if (g.n_a < 2) return MUSE_ERR_UNSUPPORTED_SHAPE;
+  if (args.route_inline &&
+      (args.n_pairs > kMaxInlinePairs || args.n_box > kMaxInlineBox || !args.ids || !args.pair_order ||
+       !args.pair_row))
+    return MUSE_ERR_UNSUPPORTED_SHAPE;
   const size_t smem = gemm_smem_bytes(args.n_box, args.stages);
   if (pick_pipes(args.n_box) == 3)
-    expert_gemm_tc<3><<<g_num_sms[dev], Variant<3>::kThreads, smem, stream>>>(tmap_b, args);
+    expert_gemm_tc<3><<<g_num_sms[dev], Variant<3>::kThreads, smem, stream>>>(tmap_b, tmap_x, args);
   else
-    expert_gemm_tc<2><<<g_num_sms[dev], Variant<2>::kThreads, smem, stream>>>(tmap_b, args);
+    expert_gemm_tc<2><<<g_num_sms[dev], Variant<2>::kThreads, smem, stream>>>(tmap_b, tmap_x, args);
   return last_launch_status();
 }
 

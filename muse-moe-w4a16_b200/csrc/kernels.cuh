@@ -22,7 +22,7 @@ struct Scratch {
   uint16_t* xs;         // bf16 [T*K, H]  hidden states gathered into expert-grouped pair order
   uint16_t* inter;      // bf16 [T*K, I]  SiLU(gate)*up per pair, expert-grouped rows
   float* ypart;         // fp32 [T*K, H]  y * (1 + post_norm_w) per pair
-  float* ssq;           // fp32 [T*K]     sum over H of ypart^2 per pair
+  float* ssq;           // fp32 [T*K, H/32] sum of ypart^2 over each 32-column slice
   int* error_flag;      // set by a kernel whose bounded wait expired
 };
 
@@ -39,7 +39,7 @@ struct ExpertWeights {
 
 // Arguments of one expert-GEMM launch (gemm_tc.cu).
 struct GemmArgs {
-  const int32_t* offsets;  // [n_local + 1] expert ranges of the pair rows
+  int32_t* offsets;        // [n_local + 1] expert ranges of the pair rows (written if route_inline)
   int n_local;
   int m_tiles;             // weight rows per expert / 128
   int k_chunks;            // K / 128
@@ -56,7 +56,20 @@ struct GemmArgs {
   float* ssq;
   int* error_flag;
   uint32_t mul16, mul64;   // 16 and 64, passed at run time (see dequant8 in gemm_tc.cu)
+  // Small batches, first GEMM only: every CTA groups the pairs itself in its prologue (CTA 0
+  // publishes offsets / pair_order / pair_row for the later kernels) and gathers activation
+  // rows straight from x by token index (tmap_x, one-row box), so no route or gather launch runs.
+  int route_inline;
+  const int32_t* ids;      // [n_pairs] expert ids (route_inline)
+  int n_pairs, local_start, top_k;
+  int32_t* pair_order;
+  int32_t* pair_row;
 };
+
+// Largest batch (tokens x top_k) whose routing the first GEMM does in its own prologue, and
+// the largest token tile it gathers row by row.
+constexpr int kMaxInlinePairs = 1024;
+constexpr int kMaxInlineBox = 32;
 
 int launch_route(const int32_t* ids, int tokens, int top_k, int local_start, int local_count,
                  int32_t* offsets, int32_t* pair_order, int32_t* pair_row, cudaStream_t stream);
@@ -66,7 +79,8 @@ int launch_gather(const uint16_t* x, const int32_t* offsets, const int32_t* pair
 
 size_t gemm_smem_bytes(int n_box, int stages);
 int pick_stages(int n_box);
-int launch_expert_gemm(const CUtensorMap& tmap_b, const GemmArgs& args, cudaStream_t stream);
+int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, const GemmArgs& args,
+                       cudaStream_t stream);
 
 // Address of the sticky device status word (current device) and a synchronous read of it.
 int device_status_ptr(int** ptr);
@@ -80,7 +94,7 @@ int launch_prepare_tiles(const uint8_t* codes, const uint8_t* scales, int n_expe
                          cudaStream_t stream);
 
 // 2-D bf16 tensor map over a row-major [rows, cols] matrix, box = 64 columns x box_rows,
-// 128-byte swizzle, zero fill out of bounds.
+// 128-byte swizzle, zero fill out of bounds (box_rows = 1 for four-row gathers).
 int make_bf16_tmap(CUtensorMap* map, const void* base, int rows, int cols, int box_rows);
 
 }  // namespace muse

@@ -11,6 +11,7 @@ workspace), so it can be captured in a CUDA graph after one eager call.
 
 from __future__ import annotations
 
+import ctypes
 import weakref
 from typing import TypedDict
 
@@ -86,9 +87,12 @@ def prepare(weights: Weights) -> dict:
 
 
 def kernel_fn(data: Inputs, state: dict, out: torch.Tensor | None = None,
-              workspace: torch.Tensor | None = None) -> torch.Tensor:
+              workspace: torch.Tensor | None = None,
+              stage_events: list | None = None) -> torch.Tensor:
     """One routed-expert layer call (baseline.py:106-151): returns bf16 [T, H] on the GPU.
-    `out` and `workspace` (uint8, >= workspace_size bytes) may be supplied by the caller."""
+    `out` and `workspace` (uint8, >= workspace_size bytes) may be supplied by the caller.
+    `stage_events` (five torch.cuda.Event(enable_timing=True)) are recorded around the kernels:
+    start, before GEMM1, after GEMM1, after GEMM2, after the combine."""
     cfg = data["config"]
     x = data["hidden_states"]
     _require_cuda(x, "hidden_states")
@@ -116,12 +120,22 @@ def kernel_fn(data: Inputs, state: dict, out: torch.Tensor | None = None,
         ws, ws_bytes = workspace, workspace.numel() * workspace.element_size()
     w13_e, w13sf_e = 2 * I * H // 2, 2 * I * H // 16     # bytes per expert
     w2_e, w2sf_e = H * I // 2, H * I // 16
-    _lib.call("muse_moe_forward", _ptr(x), _ptr(ids), _ptr(wts), T, K, lo, cnt, H, I,
-              _ptr(state["w13"], lo * w13_e), _ptr(state["w13_sf"], lo * w13sf_e),
-              _ptr(state["w13_gs"], lo * 4),
-              _ptr(state["w2"], lo * w2_e), _ptr(state["w2_sf"], lo * w2sf_e),
-              _ptr(state["w2_gs"], lo * 4),
-              _ptr(state["post_norm_w"]), _ptr(out), _ptr(ws), ws_bytes, _stream(dev))
+    args = (_ptr(x), _ptr(ids), _ptr(wts), T, K, lo, cnt, H, I,
+            _ptr(state["w13"], lo * w13_e), _ptr(state["w13_sf"], lo * w13sf_e),
+            _ptr(state["w13_gs"], lo * 4),
+            _ptr(state["w2"], lo * w2_e), _ptr(state["w2_sf"], lo * w2sf_e),
+            _ptr(state["w2_gs"], lo * 4),
+            _ptr(state["post_norm_w"]), _ptr(out), _ptr(ws), ws_bytes, _stream(dev))
+    if stage_events is None:
+        _lib.call("muse_moe_forward", *args)
+    else:
+        if len(stage_events) != 5:
+            raise _lib.MuseError(_lib.MUSE_ERR_INVALID_ARGUMENT, "stage_events needs five CUDA events")
+        for e in stage_events:   # torch creates the CUDA event on its first record
+            if not e.cuda_event:
+                e.record()
+        ev = (ctypes.c_void_p * 5)(*(e.cuda_event for e in stage_events))
+        _lib.call("muse_moe_forward_profiled", *args, ev)
     return out
 
 

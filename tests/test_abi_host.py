@@ -96,3 +96,25 @@ def test_product_path_does_not_import_oracle():
     for f in pkg_dir.rglob("*.py"):
         for line in f.read_text().splitlines():
             assert not re.match(r"\s*(from|import)\s+oracle\b", line), f"{f.name}: {line}"
+
+
+@pytest.mark.parametrize("T,K,E,H,I,launches,inline", [
+    (1, 8, 128, 2048, 768, 3, True), (32, 8, 128, 2048, 768, 3, True),
+    (128, 8, 256, 7168, 2048, 3, True), (129, 8, 256, 7168, 2048, 5, False),
+    (128, 8, 32, 4096, 4096, 5, False), (4, 8, 32, 4096, 4096, 3, True), (0, 8, 32, 4096, 4096, 0, True),
+])
+def test_launch_plan(pkg, T, K, E, H, I, launches, inline):
+    """Batches of <= 1024 pairs whose token tile is <= 32 run three kernels (routing and the
+    activation gather inside GEMM1); everything else runs route, gather, GEMM1, GEMM2, combine."""
+    from muse_moe_w4a16_b200 import _lib
+    plan = _lib.launch_plan(T, K, E, H, I)
+    assert plan["launches"] == launches and plan["route_inline"] == inline
+    assert plan["n_box"] in (16, 32, 64, 128) and plan["stages"] >= 2
+
+
+def test_profiled_forward_rejects_missing_events(lib):
+    from muse_moe_w4a16_b200 import _lib
+    ev = (ctypes.c_void_p * 5)(1, 2, 3, 4, None)
+    args = [None] * 3 + [1, 2, 0, 8, 256, 256] + [None] * 9 + [0, None]
+    assert lib.muse_moe_forward_profiled(*args, None) == _lib.MUSE_ERR_INVALID_ARGUMENT
+    assert lib.muse_moe_forward_profiled(*args, ev) == _lib.MUSE_ERR_INVALID_ARGUMENT

@@ -178,3 +178,17 @@ def test_route_oracle_is_reference_order(T, K, E, lo, cnt):
     assert offsets[-1] == order.size
     assert (row[order] == np.arange(order.size)).all()
     assert (row >= 0).sum() == order.size
+
+
+def test_package_byte_model_matches_oracle(pkg):
+    """The benchmark's byte/FLOP model (package side) equals the oracle's statement of it."""
+    from muse_moe_w4a16_b200 import traffic
+    rng = np.random.default_rng(3)
+    for T, K, E, lo, cnt in [(1, 8, 128, 0, 128), (33, 8, 256, 32, 32), (300, 2, 8, 0, 8)]:
+        ids = np.stack([rng.choice(E, K, replace=False) for _ in range(T)]).astype(np.int32)
+        for H, I in [(2048, 768), (256, 128)]:
+            assert traffic.layer_bytes(ids, lo, cnt, H, I) == orc.algorithmic_bytes(ids, lo, cnt, H, I)
+            assert traffic.layer_flops(ids, lo, cnt, H, I) == orc.algorithmic_flops(ids, lo, cnt, H, I)
+            g1 = traffic.gemm1_bytes(ids, lo, cnt, H, I)
+            g2 = traffic.gemm2_bytes(ids, lo, cnt, H, I)
+            assert g1 > 0 and g2 > 0
