@@ -41,6 +41,7 @@ typedef struct CUstream_st* muse_stream_t; /* == cudaStream_t */
 #define MUSE_ERR_WORKSPACE_TOO_SMALL (-3) /* workspace smaller than muse_moe_workspace_size   */
 #define MUSE_ERR_NO_DEVICE          (-4)  /* no sm_100 device current                          */
 #define MUSE_ERR_DEVICE_TIMEOUT     (-5)  /* a bounded device-side wait expired                */
+#define MUSE_ERR_SCRATCH_LIMIT      (-6)  /* muse_moe_forward_noalloc: needs > its 32 MiB      */
 
 /* Library version, (major << 16) | minor. */
 int muse_moe_version(void);
@@ -141,6 +142,32 @@ int muse_moe_forward_profiled(const void* x, const int32_t* topk_ids, const floa
  */
 int muse_moe_launch_plan(int tokens, int top_k, int local_count, int hidden, int inter,
                          int* plan);
+
+/*
+ * muse_moe_forward without a workspace argument: it allocates nothing and takes its scratch
+ * from a fixed 32 MiB array in device global memory that the library owns. For callers that
+ * cannot allocate device memory -- code running inside another runtime's execution callback
+ * (an inference server's plugin or custom-op hook) whose host framework owns all device
+ * allocations, or a serving loop that must not call cudaMalloc/cudaFree because they can
+ * synchronise the device. No counterpart in the reference (its kernel_fn allocates through
+ * torch); it replaces nothing.
+ *   - Calls needing more than 32 MiB of scratch (muse_moe_workspace_size) are refused with
+ *     MUSE_ERR_SCRATCH_LIMIT before any launch; decode-sized batches fit (top-8: up to 87
+ *     tokens at H = 7168, I = 2048; up to 297 at H = 2048, I = 768).
+ *   - A device holds the 32 MiB from the first call on it until the process exits. That first
+ *     call looks up the array's device address, with the device current; make it before any
+ *     stream capture.
+ *   - All calls on a device share the array and it keeps the last call's contents. Nothing in
+ *     it needs to start at zero (every value a call reads, the same call wrote first), but
+ *     calls that overlap on the GPU race on it: serialise them.
+ * Same results as muse_moe_forward.
+ */
+int muse_moe_forward_noalloc(const void* x, const int32_t* topk_ids, const float* topk_weights,
+                             int tokens, int top_k, int local_start, int local_count,
+                             int hidden, int inter,
+                             const uint8_t* w13p, const uint8_t* w13_sfp, const float* w13_gs,
+                             const uint8_t* w2p, const uint8_t* w2_sfp, const float* w2_gs,
+                             const void* post_norm_w, void* out, muse_stream_t stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

@@ -30,6 +30,8 @@ SIGNATURES: dict[str, tuple] = {
                                        _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P,
                                        ctypes.POINTER(_P)]),
     "muse_moe_launch_plan": (_I, [_I, _I, _I, _I, _I, ctypes.POINTER(_I)]),
+    "muse_moe_forward_noalloc": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I,
+                                      _P, _P, _P, _P, _P, _P, _P, _P, _P]),
 }
 
 # Return codes (include/muse_moe.h).
@@ -39,6 +41,7 @@ MUSE_ERR_UNSUPPORTED_SHAPE = -2
 MUSE_ERR_WORKSPACE_TOO_SMALL = -3
 MUSE_ERR_NO_DEVICE = -4
 MUSE_ERR_DEVICE_TIMEOUT = -5
+MUSE_ERR_SCRATCH_LIMIT = -6
 
 
 class MuseError(RuntimeError):

@@ -101,6 +101,9 @@ extern "C" const char* muse_moe_error_string(int code) {
     case MUSE_ERR_WORKSPACE_TOO_SMALL: return "workspace smaller than muse_moe_workspace_size()";
     case MUSE_ERR_NO_DEVICE: return "no sm_100 CUDA device / driver entry point available";
     case MUSE_ERR_DEVICE_TIMEOUT: return "a bounded device-side wait expired";
+    case MUSE_ERR_SCRATCH_LIMIT:
+      return "muse_moe_forward_noalloc: the call needs more scratch than its fixed 32 MiB array "
+             "(use muse_moe_forward with a caller-supplied workspace)";
     default: break;
   }
   if (code > 0) return cudaGetErrorString((cudaError_t)code);
