@@ -67,7 +67,7 @@ struct PipeCtl {
 struct SharedCtl {
   PipeCtl pipe[kMaxPipes];
   uint32_t tmem_base;
-  int total_items;
+  int item_warp_sum[8];              // items of experts [32w, 32w + 32)
   int item_prefix[kMaxExperts + 1];  // cumulative items per expert
   int ntiles[kMaxExperts];           // token tiles per expert
   uint32_t scale_lut[256];           // e4m3 byte -> bf16x2 (sf * 2^60, sf * 2^60)
@@ -205,6 +205,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     }
     offs = ctl.offs;
   }
+  int incl = 0;  // items of experts [32 * warp, threadIdx.x], threads < 256
   if (threadIdx.x < 256) {
     const float f = e4m3_to_float(threadIdx.x) * 1152921504606846976.0f;  // * 2^60
     const __nv_bfloat16 h = __float2bfloat16_rn(f);
@@ -216,13 +217,13 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     if (e < n_local) cnt = offs[e + 1] - offs[e];
     const int nt = (cnt + n_box - 1) / n_box;
     if (e < n_local) ctl.ntiles[e] = nt;
-    int incl = nt * a.m_tiles;
+    incl = nt * a.m_tiles;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
       const int o = __shfl_up_sync(0xffffffffu, incl, d);
       if (lane >= d) incl += o;
     }
-    ctl.item_prefix[e + 1] = incl;
+    if (lane == 31) ctl.item_warp_sum[warp] = incl;
   }
   if (warp == kMmaWarp0) {
     ptx::tmem_alloc(&ctl.tmem_base, kTmemCols);
@@ -235,20 +236,16 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     for (int i = threadIdx.x; i < a.n_pairs; i += R::kThreads)
       if (ctl.order[i] >= 0) ctl.order[i] /= a.top_k;
   }
-  if (threadIdx.x == 0) {
-    ctl.item_prefix[0] = 0;
-    int carry = 0;
-    for (int w = 0; w < 8; ++w) {
-      const int last = ctl.item_prefix[32 * w + 32];
-      for (int i = 1; i <= 32; ++i) ctl.item_prefix[32 * w + i] += carry;
-      carry += last;
-    }
-    ctl.total_items = ctl.item_prefix[n_local];
+  if (threadIdx.x < 256) {  // complete the scan across the 8 warps
+    int before = 0;
+    for (int w = 0; w < warp; ++w) before += ctl.item_warp_sum[w];
+    ctl.item_prefix[threadIdx.x + 1] = before + incl;
+    if (threadIdx.x == 0) ctl.item_prefix[0] = 0;
   }
   __syncthreads();
 
   const uint32_t tbase = ctl.tmem_base;
-  const int total = ctl.total_items;
+  const int total = ctl.item_prefix[n_local];
   const int G = gridDim.x;
   const int kcn = a.k_chunks;
   // Tile j of this CTA is item blockIdx.x + j * G. Its K chunks are split over the pipelines
