@@ -10,9 +10,10 @@ I=768; T in {1, 4, 16, 32}; uniform router; NVFP4 weights from N(0, 0.02)).
 A step is one layer call at every token count of the sweep. Each call is a CUDA-graph
 replay of kernel_fn, preceded (outside its timing) by a 512 MiB write that flushes the L2,
 and timed with CUDA events on the launching stream. `value` is the geometric mean over the
-sweep of the mean us/call; `per_T` lists each token count. Under torchrun every rank runs
-the same single-GPU workload (a replica; the layer's decode path has no data exchange) and
-times are the max over ranks.
+sweep of the mean us/call; `per_T` lists each token count. Under torchrun (N > 1) the layer
+runs expert-parallel: each rank holds E/N experts, every rank sees all tokens (the decode
+layout), the fp32 shares are all-reduced over NCCL inside the captured graph, and times are the
+max over ranks (strong scaling: the same call, split N ways).
 
 `--impl reference` times the CPU oracle (the reference's fp32 dequantise-then-accumulate
 path restated in numpy, all host cores) on the same workload; rank 0 only.
@@ -225,7 +226,8 @@ def config_block(args, shape, tokens):
                         f"router={shape.router} T={list(tokens)}",
             "weights": "NVFP4 (e2m1, e4m3 block-16 scales, fp32 global scale) from N(0,0.02)",
             "activations": "bf16 N(0,1)", "l2": "flushed by a 512 MiB write before every timed call",
-            "parallelism": f"replicas x{args.gpus}" if args.gpus > 1 else "single GPU"}
+            "parallelism": (f"ep{args.gpus}: experts split in contiguous blocks, tokens replicated, "
+                            "fp32 shares all-reduced over NCCL") if args.gpus > 1 else "single GPU"}
 
 
 # ----------------------------------------------------------------------------- CPU baseline leg
@@ -250,6 +252,16 @@ def cpu_baseline(shape, tokens, w, inputs):
 
 # ----------------------------------------------------------------------------- our arm
 
+class _Eager:
+    """Stands in for a captured graph: replay() launches the call eagerly."""
+
+    def __init__(self, fn):
+        self.fn = fn
+
+    def replay(self):
+        self.fn()
+
+
 def run_muse(args, world, rank, local):
     pkg = __graft_entry__.load_package()
     from muse_moe_w4a16_b200 import _lib, synth, traffic
@@ -257,21 +269,36 @@ def run_muse(args, world, rank, local):
     dev = torch.device("cuda", local)
     shape, tokens = workload(args, synth)
     w = synth.baseline_weights(shape, seed=synth.WEIGHTS_SEED, device=dev)
-    state = pkg.prepare(w)
+    if world > 1:
+        # expert-parallel: this rank repacks and computes only its block of experts; every
+        # rank holds all tokens (decode layout) and the fp32 shares are all-reduced over NCCL
+        from muse_moe_w4a16_b200 import ep
+        moe = ep.ExpertParallelMoE(w)
+        layer_call = moe.forward_replicated
+        experts = moe.experts
+    else:
+        state = pkg.prepare(w)
+        layer_call = lambda d: pkg.kernel_fn(d, state)  # noqa: E731
+        experts = range(shape.local_start, shape.local_start + shape.n_local)
     inputs = {t: synth.baseline_input(shape, t, seed=input_seed(args.workload, t)) for t in tokens}
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    # Device-resident inputs and one captured graph per token count.
+    # Device-resident inputs and one captured graph per token count. With N > 1 the calls
+    # contain NCCL collectives, which stay out of graphs: they are launched eagerly (the flush
+    # in front of each call keeps the GPU behind the host, so launch gaps do not show).
     graphs, outs, dev_in = {}, {}, {}
     for t in tokens:
         d = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in inputs[t].items()}
         dev_in[t] = d
-        pkg.kernel_fn(d, state)          # eager first call (kernel attributes)
+        outs[t] = layer_call(d)          # eager first call (kernel attributes, communicator)
         torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
-            outs[t] = pkg.kernel_fn(d, state)
+        if world == 1:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                outs[t] = layer_call(d)
+        else:
+            g = _Eager(lambda d=d: layer_call(d))
         graphs[t] = g
 
     # End-to-end graphs: pinned host inputs -> device, kernel_fn, result -> pinned host.
@@ -284,14 +311,20 @@ def run_muse(args, world, rank, local):
         d = {k: (torch.empty_like(v, device=dev) if isinstance(v, torch.Tensor) else v) for k, v in hi.items()}
         for k in ("hidden_states", "topk_ids", "topk_weights"):
             d[k].copy_(hi[k], non_blocking=True)
-        pkg.kernel_fn(d, state)
+        layer_call(d)
         torch.cuda.synchronize()
-        g = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(g):
+
+        def e2e_step(d=d, hi=hi, ho=host_out[t]):
             for k in ("hidden_states", "topk_ids", "topk_weights"):
                 d[k].copy_(hi[k], non_blocking=True)
-            o = pkg.kernel_fn(d, state)
-            host_out[t].copy_(o, non_blocking=True)
+            ho.copy_(layer_call(d), non_blocking=True)
+
+        if world == 1:
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                e2e_step()
+        else:
+            g = _Eager(e2e_step)
         e2e_graphs[t] = g
         h2d += sum(hi[k].numel() * hi[k].element_size() for k in ("hidden_states", "topk_ids", "topk_weights"))
         d2h += host_out[t].numel() * 2
@@ -325,16 +358,18 @@ def run_muse(args, world, rank, local):
     # 512 MiB flush in front of each call keeps the GPU behind the host, so no event waits on
     # a launch). [0]->[1] route + gather (empty when GEMM1 routes), [1]->[2] GEMM1,
     # [2]->[3] GEMM2, [3]->[4] combine.
-    stage = {t: [] for t in tokens}
-    for i in range(args.steps):
-        for t in tokens:
-            evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
-            flush.zero_()
-            pkg.kernel_fn(dev_in[t], state, out=outs[t], stage_events=evs)
-            stage[t].append(evs)
-    torch.cuda.synchronize()
-    stage_us = {t: [statistics.mean(e[j].elapsed_time(e[j + 1]) * 1e3 for e in stage[t]) for j in range(4)]
-                for t in tokens}
+    stage_us = {t: [0.0, 0.0, 0.0, 0.0] for t in tokens}
+    if world == 1:
+        stage = {t: [] for t in tokens}
+        for i in range(args.steps):
+            for t in tokens:
+                evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+                flush.zero_()
+                pkg.kernel_fn(dev_in[t], state, out=outs[t], stage_events=evs)
+                stage[t].append(evs)
+        torch.cuda.synchronize()
+        stage_us = {t: [statistics.mean(e[j].elapsed_time(e[j + 1]) * 1e3 for e in stage[t]) for j in range(4)]
+                    for t in tokens}
 
     per_t = [statistics.mean(a.elapsed_time(b) * 1e3 for a, b in ev[t]) for t in tokens]
     per_t_e2e = [statistics.mean(a.elapsed_time(b) * 1e3 for a, b in ev_e2e[t]) for t in tokens]
@@ -343,7 +378,6 @@ def run_muse(args, world, rank, local):
     flat = max_over_ranks(world, [v for t in tokens for v in stage_us[t]])
     stage_us = {t: flat[4 * i:4 * i + 4] for i, t in enumerate(tokens)}
 
-    # Correctness of what was timed: the graph outputs against the oracle (cheap sizes only).
     pk = peaks()
     dims = (shape.local_start, shape.n_local, shape.hidden, shape.inter)
     per_rows = []
@@ -356,36 +390,49 @@ def run_muse(args, world, rank, local):
         b1 = traffic.gemm1_bytes(ids, *dims)
         b2 = traffic.gemm2_bytes(ids, *dims)
         pre, k1, k2, comb = stage_us[t]
-        plan = _lib.launch_plan(t, shape.top_k, shape.n_local, shape.hidden, shape.inter)
-        launches_per_step += plan["launches"]
+        plan = _lib.launch_plan(t, shape.top_k, len(experts), shape.hidden, shape.inter)
+        launches_per_step += plan["launches"] + (1 if world > 1 else 0)   # + the bf16 cast
         gbs = b / (us * 1e-6) / 1e9
         g1_bytes += b1
         g1_time += k1
-        per_rows.append({"T": t, "us": round(us, 3), "bytes": b, "flops": f, "GBps": round(gbs, 1),
-                         "hbm_frac": round(gbs / pk["hbm_gbs"], 4),
-                         "roofline_us": round(max(b / pk["hbm_gbs"] / 1e3, f / pk["bf16_tflops"] / 1e6), 3),
-                         "kernels_us": {"route_gather": round(pre, 3), "gemm1": round(k1, 3),
-                                        "gemm2": round(k2, 3), "combine": round(comb, 3)},
-                         "gemm1_GBps": round(b1 / (k1 * 1e-6) / 1e9, 1),
-                         "gemm2_GBps": round(b2 / (k2 * 1e-6) / 1e9, 1),
-                         "launches": plan["launches"], "n_box": plan["n_box"],
-                         "route_inline": plan["route_inline"]})
-    achieved = g1_bytes / (g1_time * 1e-6) / 1e9
+        row = {"T": t, "us": round(us, 3), "bytes": b, "flops": f, "GBps": round(gbs, 1),
+               "hbm_frac": round(gbs / (pk["hbm_gbs"] * world), 4),
+               "roofline_us": round(max(b / (pk["hbm_gbs"] * world) / 1e3,
+                                        f / (pk["bf16_tflops"] * world) / 1e6), 3),
+               "launches": plan["launches"], "n_box": plan["n_box"], "route_inline": plan["route_inline"]}
+        if world == 1:   # per-kernel event times (single-GPU calls only)
+            row.update({"kernels_us": {"route_gather": round(pre, 3), "gemm1": round(k1, 3),
+                                       "gemm2": round(k2, 3), "combine": round(comb, 3)},
+                        "gemm1_GBps": round(b1 / (k1 * 1e-6) / 1e9, 1),
+                        "gemm2_GBps": round(b2 / (k2 * 1e-6) / 1e9, 1)})
+        per_rows.append(row)
+    if world == 1:
+        achieved = g1_bytes / (g1_time * 1e-6) / 1e9
+        roof_kernel = ("expert_gemm_tc, GEMM1 launch (w13 + SiLU*up): algorithmic bytes per "
+                       "launch / mean CUDA-event duration, summed over the token sweep")
+        roof_peak = pk["hbm_gbs"]
+    else:
+        # whole expert-parallel call: every rank's algorithmic bytes over the slowest rank's
+        # time, against N GPUs' bandwidth
+        achieved = sum(r["bytes"] for r in per_rows) / (sum(per_t) * 1e-6) / 1e9
+        roof_kernel = (f"whole expert-parallel layer call over {world} GPUs (local GEMMs + combine + "
+                       f"NCCL all-reduce + cast), sweep aggregate, against {world} x HBM peak")
+        roof_peak = pk["hbm_gbs"] * world
     line = {
         "metric": metric_name(args), "value": round(geomean(per_t), 3), "unit": "us/call",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": round(sum(per_t) / 1e3, 5), "higher_is_better": False, "scaling": "weak",
+        "ms_per_step": round(sum(per_t) / 1e3, 5), "higher_is_better": False,
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; random-init NVFP4 weights)",
         "config": config_block(args, shape, tokens),
         "per_T": per_rows,
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": pk["hbm_gbs"], "unit": "GB/s",
-                     "frac": round(achieved / pk["hbm_gbs"], 4), "traffic": None,
-                     "peak_source": pk["source"],
-                     "kernel": "expert_gemm_tc, GEMM1 launch (w13 + SiLU*up): algorithmic bytes per "
-                               "launch / mean CUDA-event duration, summed over the token sweep"},
+        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": roof_peak, "unit": "GB/s",
+                     "frac": round(achieved / roof_peak, 4), "traffic": None,
+                     "peak_source": pk["source"], "kernel": roof_kernel},
         "e2e": {"value": round(geomean(per_t_e2e), 3), "unit": "us/call", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h,
-                "how": "CUDA graph of pinned-host->device copies, kernel_fn, device->pinned-host copy"},
+                "how": ("CUDA graph of " if world == 1 else "eager ") +
+                       "pinned-host->device copies, layer call, device->pinned-host copy"},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": clocks.summary(),
     }
@@ -393,6 +440,8 @@ def run_muse(args, world, rank, local):
         line["cpu_baseline"] = cpu_baseline(shape, tokens, w, inputs)
     if rank == 0:
         print(json.dumps(line), flush=True)
+    del graphs, e2e_graphs   # graphs holding NCCL calls go before the process group
+    torch.cuda.synchronize()
     return 0
 
 

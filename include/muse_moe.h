@@ -118,6 +118,30 @@ int muse_moe_forward(const void* x, const int32_t* topk_ids, const float* topk_w
                      void* workspace, size_t workspace_bytes, muse_stream_t stream);
 
 /*
+ * One expert-parallel rank's share of the layer: muse_moe_forward for the local experts
+ * [local_start, local_start + local_count), but `out_f32` (fp32 [T, H]) receives the fp32 sum
+ * over this rank's local slots of topk_weight * norm(y), before any bf16 rounding (zeros for
+ * tokens with no local pair). Summing out_f32 over all ranks and casting to bf16
+ * (muse_moe_cast_bf16) gives muse_moe_forward's output for the whole expert range. Replaces the
+ * per-GPU part of the reference's ep8 layer (reference.py:18-22, TASK.md:29: each GPU computes
+ * only its local experts' pairs); the cross-rank sum is the caller's collective.
+ */
+int muse_moe_forward_partial(const void* x, const int32_t* topk_ids, const float* topk_weights,
+                             int tokens, int top_k, int local_start, int local_count,
+                             int hidden, int inter,
+                             const uint8_t* w13p, const uint8_t* w13_sfp, const float* w13_gs,
+                             const uint8_t* w2p, const uint8_t* w2_sfp, const float* w2_gs,
+                             const void* post_norm_w, float* out_f32,
+                             void* workspace, size_t workspace_bytes, muse_stream_t stream);
+
+/*
+ * out[i] = bf16(in[i]) (round to nearest even) for n fp32 values; n a multiple of 8, both
+ * pointers 16-byte aligned. The final cast of an expert-parallel layer's summed partials
+ * (reference.py:107, the bf16 cast of the fp32 accumulator).
+ */
+int muse_moe_cast_bf16(const float* in, void* out, size_t n, muse_stream_t stream);
+
+/*
  * muse_moe_forward, with five caller-created CUDA events (cudaEvent_t, passed as void*)
  * recorded on `stream` around the kernels: [0] start, [1] before GEMM1, [2] after GEMM1,
  * [3] after GEMM2, [4] after the combine. For per-kernel timing; same results as

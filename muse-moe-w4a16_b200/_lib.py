@@ -30,6 +30,9 @@ SIGNATURES: dict[str, tuple] = {
                                        _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P,
                                        ctypes.POINTER(_P)]),
     "muse_moe_launch_plan": (_I, [_I, _I, _I, _I, _I, ctypes.POINTER(_I)]),
+    "muse_moe_forward_partial": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I,
+                                      _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P]),
+    "muse_moe_cast_bf16": (_I, [_P, _P, ctypes.c_size_t, _P]),
     "muse_moe_forward_noalloc": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I,
                                       _P, _P, _P, _P, _P, _P, _P, _P, _P]),
 }

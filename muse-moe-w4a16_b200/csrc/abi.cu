@@ -163,7 +163,7 @@ int forward_impl(const void* x, const int32_t* topk_ids, const float* topk_weigh
                  const uint8_t* w13p, const uint8_t* w13_sfp, const float* w13_gs,
                  const uint8_t* w2p, const uint8_t* w2_sfp, const float* w2_gs,
                  const void* post_norm_w, void* out, void* workspace, size_t workspace_bytes,
-                 cudaStream_t st, cudaEvent_t* ev) {
+                 cudaStream_t st, cudaEvent_t* ev, bool f32_out = false) {
   int rc = check_dims(tokens, top_k, local_start, local_count, hidden, inter);
   if (rc) return rc;
   if (tokens == 0) return MUSE_OK;
@@ -256,7 +256,7 @@ int forward_impl(const void* x, const int32_t* topk_ids, const float* topk_weigh
   g2.route_inline = 0;
   if ((rc = launch_expert_gemm(tmap_i, tmap_i, g2, st))) return rc;
   if ((rc = mark(3))) return rc;
-  if ((rc = launch_combine(d, topk_ids, topk_weights, s, static_cast<uint16_t*>(out), st))) return rc;
+  if ((rc = launch_combine(d, topk_ids, topk_weights, s, out, f32_out, st))) return rc;
   return mark(4);
 }
 
@@ -292,6 +292,26 @@ extern "C" int muse_moe_forward_profiled(const void* x, const int32_t* topk_ids,
   return forward_impl(x, topk_ids, topk_weights, tokens, top_k, local_start, local_count, hidden,
                       inter, w13p, w13_sfp, w13_gs, w2p, w2_sfp, w2_gs, post_norm_w, out, workspace,
                       workspace_bytes, (cudaStream_t)stream, ev);
+}
+
+extern "C" int muse_moe_forward_partial(const void* x, const int32_t* topk_ids,
+                                        const float* topk_weights, int tokens, int top_k,
+                                        int local_start, int local_count, int hidden, int inter,
+                                        const uint8_t* w13p, const uint8_t* w13_sfp,
+                                        const float* w13_gs, const uint8_t* w2p,
+                                        const uint8_t* w2_sfp, const float* w2_gs,
+                                        const void* post_norm_w, float* out_f32, void* workspace,
+                                        size_t workspace_bytes, muse_stream_t stream) {
+  return forward_impl(x, topk_ids, topk_weights, tokens, top_k, local_start, local_count, hidden,
+                      inter, w13p, w13_sfp, w13_gs, w2p, w2_sfp, w2_gs, post_norm_w, out_f32,
+                      workspace, workspace_bytes, (cudaStream_t)stream, nullptr, true);
+}
+
+extern "C" int muse_moe_cast_bf16(const float* in, void* out, size_t n, muse_stream_t stream) {
+  if (n == 0) return MUSE_OK;
+  if (!in || !out || n % 8 || reinterpret_cast<uintptr_t>(in) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+    return MUSE_ERR_INVALID_ARGUMENT;
+  return launch_cast_bf16(in, static_cast<uint16_t*>(out), n, (cudaStream_t)stream);
 }
 
 extern "C" int muse_moe_launch_plan(int tokens, int top_k, int local_count, int hidden, int inter,

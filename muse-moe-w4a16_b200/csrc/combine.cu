@@ -16,10 +16,12 @@ constexpr int kThreads = 128;
 constexpr int kColsPerCta = kThreads * 4;
 
 // grid (tokens, ceil(H / 512)). Warp w reduces the slice sums of slots w, w + 4, ...
+// kF32Out: write the fp32 sum (an expert-parallel rank's partial) instead of bf16.
+template <bool kF32Out>
 __global__ void __launch_bounds__(kThreads)
 combine_kernel(const int32_t* __restrict__ ids, const float* __restrict__ topk_weights,
                const int32_t* __restrict__ pair_row, const float* __restrict__ ypart,
-               const float* __restrict__ ssq, int top_k, int H, uint16_t* __restrict__ out) {
+               const float* __restrict__ ssq, int top_k, int H, void* __restrict__ out) {
   __shared__ int s_row[kMaxTopK], s_key[kMaxTopK];
   __shared__ float s_coef[kMaxTopK];
   __shared__ int s_order[kMaxTopK];
@@ -71,21 +73,49 @@ combine_kernel(const int32_t* __restrict__ ids, const float* __restrict__ topk_w
     acc.z = fmaf(c, v.z, acc.z);
     acc.w = fmaf(c, v.w, acc.w);
   }
-  __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
-  __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
-  uint2 packed;
-  packed.x = *reinterpret_cast<uint32_t*>(&lo);
-  packed.y = *reinterpret_cast<uint32_t*>(&hi);
-  reinterpret_cast<uint2*>(out + (size_t)t * H)[h4] = packed;
+  if (kF32Out) {
+    reinterpret_cast<float4*>(static_cast<float*>(out) + (size_t)t * H)[h4] = acc;
+  } else {
+    __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
+    __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
+    uint2 packed;
+    packed.x = *reinterpret_cast<uint32_t*>(&lo);
+    packed.y = *reinterpret_cast<uint32_t*>(&hi);
+    reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + (size_t)t * H)[h4] = packed;
+  }
+}
+
+// out[i] = bf16(in[i]), 8 elements per thread (n a multiple of 8).
+__global__ void __launch_bounds__(256)
+cast_bf16_kernel(const float4* __restrict__ in, uint4* __restrict__ out, size_t n8) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n8; i += (size_t)gridDim.x * blockDim.x) {
+    const float4 a = in[2 * i], b = in[2 * i + 1];
+    __nv_bfloat162 v[4] = {__floats2bfloat162_rn(a.x, a.y), __floats2bfloat162_rn(a.z, a.w),
+                           __floats2bfloat162_rn(b.x, b.y), __floats2bfloat162_rn(b.z, b.w)};
+    out[i] = *reinterpret_cast<const uint4*>(v);
+  }
 }
 
 }  // namespace
 
 int launch_combine(const LayerDims& d, const int32_t* ids, const float* topk_weights,
-                   const Scratch& s, uint16_t* out, cudaStream_t stream) {
+                   const Scratch& s, void* out, bool f32_out, cudaStream_t stream) {
   dim3 grid(d.tokens, (d.hidden + kColsPerCta - 1) / kColsPerCta);
-  combine_kernel<<<grid, kThreads, 0, stream>>>(ids, topk_weights, s.pair_row, s.ypart, s.ssq,
-                                                d.top_k, d.hidden, out);
+  if (f32_out)
+    combine_kernel<true><<<grid, kThreads, 0, stream>>>(ids, topk_weights, s.pair_row, s.ypart,
+                                                         s.ssq, d.top_k, d.hidden, out);
+  else
+    combine_kernel<false><<<grid, kThreads, 0, stream>>>(ids, topk_weights, s.pair_row, s.ypart,
+                                                          s.ssq, d.top_k, d.hidden, out);
+  return last_launch_status();
+}
+
+int launch_cast_bf16(const float* in, uint16_t* out, size_t n, cudaStream_t stream) {
+  const size_t n8 = n / 8;
+  if (n8 == 0) return MUSE_OK;
+  const size_t blocks = (n8 + 255) / 256;
+  cast_bf16_kernel<<<blocks < 1184 ? (unsigned)blocks : 1184u, 256, 0, stream>>>(
+      reinterpret_cast<const float4*>(in), reinterpret_cast<uint4*>(out), n8);
   return last_launch_status();
 }
 

@@ -87,7 +87,10 @@ int device_status_ptr(int** ptr);
 int read_device_status(int* status, int reset);
 
 int launch_combine(const LayerDims& d, const int32_t* ids, const float* topk_weights,
-                   const Scratch& s, uint16_t* out, cudaStream_t stream);
+                   const Scratch& s, void* out, bool f32_out, cudaStream_t stream);
+
+// out[i] = bf16(in[i]) for n elements (n a multiple of 8, both 16-byte aligned).
+int launch_cast_bf16(const float* in, uint16_t* out, size_t n, cudaStream_t stream);
 
 int launch_prepare_tiles(const uint8_t* codes, const uint8_t* scales, int n_experts, int rows,
                          int k, int gate_up_inter, uint8_t* codes_out, uint8_t* scales_out,

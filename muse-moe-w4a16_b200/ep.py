@@ -1,0 +1,103 @@
+"""Expert parallelism across the GPUs of one node: one process per GPU, experts split into
+contiguous blocks, NCCL for the exchange.
+
+The reference's problem is always expert-parallel: GPU r holds experts
+[32r, 32r + 32) and computes only their (token, slot) pairs (reference.py:18-22, TASK.md:29).
+Here a rank computes the fp32 sum of its local slots for the tokens it sees
+(`kernel_fn_partial`, one CUDA launch sequence), the ranks sum those partials with one
+collective, and the result is cast to bf16 once (`cast_bf16`), so the output is the
+single-GPU layer's output up to the order of one fp32 addition per rank.
+
+Two layouts of the tokens:
+  replicated (decode): every rank holds the same T tokens. Partials [T, H] fp32 are summed
+      with an all-reduce; every rank returns the full output.
+  sharded (prefill): rank r holds its own T_r tokens (T_r equal on every rank). Inputs are
+      all-gathered (x bf16, ids, weights), every rank computes its experts' share of all
+      R * T_r tokens, and a reduce-scatter returns each rank the sum for its own tokens.
+
+Collectives use fixed shapes (no counts sent to the host), so a call issues no host
+synchronisation and can be captured in a CUDA graph together with the NCCL calls.
+"""
+
+from __future__ import annotations
+
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+from . import _lib
+from .layer import Inputs, Weights, cast_bf16, kernel_fn_partial, prepare
+
+
+def expert_block(n_experts: int, rank: int, world: int) -> range:
+    """Contiguous experts of `rank`: the first n_experts % world ranks hold one extra."""
+    if world <= 0 or not 0 <= rank < world or n_experts < world:
+        raise _lib.MuseError(_lib.MUSE_ERR_INVALID_ARGUMENT,
+                             f"cannot split {n_experts} experts over {world} ranks (rank {rank})")
+    base, extra = divmod(n_experts, world)
+    lo = rank * base + min(rank, extra)
+    return range(lo, lo + base + (1 if rank < extra else 0))
+
+
+def _with_local_range(data: Inputs, experts: range) -> Inputs:
+    cfg = dict(data["config"])
+    cfg["local_start"], cfg["local_count"] = experts.start, len(experts)
+    return {**data, "config": cfg}
+
+
+class ExpertParallelMoE:
+    """One rank of an expert-parallel layer.
+
+    `weights` may hold every expert (each rank repacks only its own block) or only this rank's
+    block, in which case pass `n_experts` (the model's expert count) and set `weights_are_local`.
+    `local_fn(data) -> fp32 [T, H]` and `cast_fn(fp32) -> bf16` default to the CUDA kernels;
+    tests replace them to check the exchange logic on CPU ranks.
+    """
+
+    def __init__(self, weights: Weights | None, group=None, *, n_experts: int | None = None,
+                 weights_are_local: bool = False,
+                 local_fn: Callable[[Inputs], torch.Tensor] | None = None,
+                 cast_fn: Callable[[torch.Tensor], torch.Tensor] | None = None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if n_experts is None:
+            n_experts = weights["w13"].shape[0]
+        self.n_experts = n_experts
+        self.experts = expert_block(n_experts, self.rank, self.world)
+        if local_fn is None:
+            if weights_are_local:
+                state = prepare(weights)
+                state["expert_base"] = self.experts.start
+            else:
+                state = prepare(weights, self.experts)
+            self.state = state
+            local_fn = lambda d: kernel_fn_partial(d, self.state)  # noqa: E731
+        self._local = local_fn
+        self._cast = cast_fn or cast_bf16
+
+    def forward_replicated(self, data: Inputs) -> torch.Tensor:
+        """Decode layout: the same T tokens on every rank -> bf16 [T, H] on every rank."""
+        part = self._local(_with_local_range(data, self.experts))
+        dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
+        return self._cast(part)
+
+    def forward_sharded(self, data: Inputs) -> torch.Tensor:
+        """Prefill layout: this rank's T_r tokens (T_r equal on every rank) -> bf16 [T_r, H],
+        the layer's output for those tokens over all experts."""
+        x, ids, wts = data["hidden_states"], data["topk_ids"], data["topk_weights"]
+        t_r = x.shape[0]
+        R = self.world
+        full = {}
+        for name, t in (("hidden_states", x), ("topk_ids", ids.to(torch.int32)),
+                        ("topk_weights", wts.to(torch.float32))):
+            t = t.contiguous()
+            g = torch.empty((R * t_r,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+            dist.all_gather_into_tensor(g, t, group=self.group)
+            full[name] = g
+        gathered = {**data, **full}
+        part = self._local(_with_local_range(gathered, self.experts))
+        mine = torch.empty((t_r, part.shape[1]), dtype=part.dtype, device=part.device)
+        dist.reduce_scatter_tensor(mine, part, op=dist.ReduceOp.SUM, group=self.group)
+        return self._cast(mine)

@@ -61,38 +61,41 @@ def _require_cuda(t: torch.Tensor, name: str) -> None:
         raise _lib.MuseError(_lib.MUSE_ERR_NO_DEVICE, f"{name} must be a CUDA tensor (no CPU path)")
 
 
-def prepare(weights: Weights) -> dict:
-    """Repack every expert's NVFP4 weights into the kernels' tile order (lossless, same bytes;
-    baseline.py:82-103). Untimed. The returned state serves any local expert range."""
+def prepare(weights: Weights, experts: range | None = None) -> dict:
+    """Repack the NVFP4 weights into the kernels' tile order (lossless, same bytes;
+    baseline.py:82-103). Untimed. The returned state serves any local expert range inside the
+    repacked experts: all of them, or only `experts` (a contiguous global range, e.g. one
+    expert-parallel rank's block) when given."""
     w13, w2 = weights["w13"], weights["w2"]
     _require_cuda(w13, "w13")
     E, two_i, h_half = w13.shape
     H, I = 2 * h_half, two_i // 2
     if tuple(w2.shape) != (E, H, I // 2):
         raise _lib.MuseError(_lib.MUSE_ERR_INVALID_ARGUMENT, f"w2 shape {tuple(w2.shape)} != {(E, H, I // 2)}")
+    sel = range(E) if experts is None else experts
+    if sel.step != 1 or not (0 <= sel.start < sel.stop <= E):
+        raise _lib.MuseError(_lib.MUSE_ERR_INVALID_ARGUMENT, f"experts {sel} is not a contiguous range of [0, {E})")
+    lo, n = sel.start, len(sel)
     dev = w13.device
     srcs = [weights["w13"], weights["w13_sf"], weights["w2"], weights["w2_sf"]]
-    srcs = [s.contiguous().view(torch.uint8) for s in srcs]
+    srcs = [s[lo:lo + n].contiguous().view(torch.uint8) for s in srcs]
     outs = [torch.empty_like(s) for s in srcs]
     with torch.cuda.device(dev):
-        _lib.call("muse_moe_prepare_weights", *[_ptr(s) for s in srcs], E, H, I,
+        _lib.call("muse_moe_prepare_weights", *[_ptr(s) for s in srcs], n, H, I,
                   *[_ptr(o) for o in outs], _stream(dev))
     return {
         "w13": outs[0], "w13_sf": outs[1], "w2": outs[2], "w2_sf": outs[3],
-        "w13_gs": weights["w13_gs"].to(device=dev, dtype=torch.float32).contiguous(),
-        "w2_gs": weights["w2_gs"].to(device=dev, dtype=torch.float32).contiguous(),
+        "w13_gs": weights["w13_gs"][lo:lo + n].to(device=dev, dtype=torch.float32).contiguous(),
+        "w2_gs": weights["w2_gs"][lo:lo + n].to(device=dev, dtype=torch.float32).contiguous(),
         "post_norm_w": weights["post_norm_w"].to(device=dev, dtype=torch.bfloat16).contiguous(),
-        "n_experts": E, "hidden": H, "inter": I,
+        "n_experts": n, "expert_base": lo, "hidden": H, "inter": I,
     }
 
 
-def kernel_fn(data: Inputs, state: dict, out: torch.Tensor | None = None,
-              workspace: torch.Tensor | None = None,
-              stage_events: list | None = None) -> torch.Tensor:
-    """One routed-expert layer call (baseline.py:106-151): returns bf16 [T, H] on the GPU.
-    `out` and `workspace` (uint8, >= workspace_size bytes) may be supplied by the caller.
-    `stage_events` (five torch.cuda.Event(enable_timing=True)) are recorded around the kernels:
-    start, before GEMM1, after GEMM1, after GEMM2, after the combine."""
+def _call_args(data: Inputs, state: dict, out: torch.Tensor | None, workspace: torch.Tensor | None,
+               out_dtype: torch.dtype):
+    """Validated pointers and sizes of one layer call (the argument list shared by
+    muse_moe_forward, _profiled and _partial), plus the output tensor."""
     cfg = data["config"]
     x = data["hidden_states"]
     _require_cuda(x, "hidden_states")
@@ -105,27 +108,43 @@ def kernel_fn(data: Inputs, state: dict, out: torch.Tensor | None = None,
     K = ids.shape[1]
     I = state["inter"]
     lo, cnt = int(cfg["local_start"]), int(cfg["local_count"])
-    if H != state["hidden"] or lo < 0 or lo + cnt > state["n_experts"] or tuple(ids.shape) != (T, K) \
-            or tuple(wts.shape) != (T, K):
+    base = int(state.get("expert_base", 0))   # global id of the state's first expert
+    if H != state["hidden"] or lo < base or lo + cnt > base + state["n_experts"] \
+            or tuple(ids.shape) != (T, K) or tuple(wts.shape) != (T, K):
         raise _lib.MuseError(_lib.MUSE_ERR_INVALID_ARGUMENT,
                              f"inconsistent shapes: x {tuple(x.shape)}, ids {tuple(ids.shape)}, "
-                             f"weights {tuple(wts.shape)}, local [{lo}, {lo + cnt}) of {state['n_experts']}")
+                             f"weights {tuple(wts.shape)}, local [{lo}, {lo + cnt}) of "
+                             f"[{base}, {base + state['n_experts']})")
     dev = x.device
     if out is None:
-        out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
+        out = torch.empty((T, H), dtype=out_dtype, device=dev)
+    elif out.dtype != out_dtype or tuple(out.shape) != (T, H) or not out.is_contiguous():
+        raise _lib.MuseError(_lib.MUSE_ERR_INVALID_ARGUMENT, f"out must be a contiguous {out_dtype} [{T}, {H}]")
     ws_bytes = _lib.workspace_size(T, K, cnt, H, I)
     if workspace is None:
         ws = torch.empty((max(ws_bytes, 1),), dtype=torch.uint8, device=dev)
     else:
         ws, ws_bytes = workspace, workspace.numel() * workspace.element_size()
+    e0 = lo - base
     w13_e, w13sf_e = 2 * I * H // 2, 2 * I * H // 16     # bytes per expert
     w2_e, w2sf_e = H * I // 2, H * I // 16
     args = (_ptr(x), _ptr(ids), _ptr(wts), T, K, lo, cnt, H, I,
-            _ptr(state["w13"], lo * w13_e), _ptr(state["w13_sf"], lo * w13sf_e),
-            _ptr(state["w13_gs"], lo * 4),
-            _ptr(state["w2"], lo * w2_e), _ptr(state["w2_sf"], lo * w2sf_e),
-            _ptr(state["w2_gs"], lo * 4),
+            _ptr(state["w13"], e0 * w13_e), _ptr(state["w13_sf"], e0 * w13sf_e),
+            _ptr(state["w13_gs"], e0 * 4),
+            _ptr(state["w2"], e0 * w2_e), _ptr(state["w2_sf"], e0 * w2sf_e),
+            _ptr(state["w2_gs"], e0 * 4),
             _ptr(state["post_norm_w"]), _ptr(out), _ptr(ws), ws_bytes, _stream(dev))
+    return args, out
+
+
+def kernel_fn(data: Inputs, state: dict, out: torch.Tensor | None = None,
+              workspace: torch.Tensor | None = None,
+              stage_events: list | None = None) -> torch.Tensor:
+    """One routed-expert layer call (baseline.py:106-151): returns bf16 [T, H] on the GPU.
+    `out` and `workspace` (uint8, >= workspace_size bytes) may be supplied by the caller.
+    `stage_events` (five torch.cuda.Event(enable_timing=True)) are recorded around the kernels:
+    start, before GEMM1, after GEMM1, after GEMM2, after the combine."""
+    args, out = _call_args(data, state, out, workspace, torch.bfloat16)
     if stage_events is None:
         _lib.call("muse_moe_forward", *args)
     else:
@@ -136,6 +155,27 @@ def kernel_fn(data: Inputs, state: dict, out: torch.Tensor | None = None,
                 e.record()
         ev = (ctypes.c_void_p * 5)(*(e.cuda_event for e in stage_events))
         _lib.call("muse_moe_forward_profiled", *args, ev)
+    return out
+
+
+def kernel_fn_partial(data: Inputs, state: dict, out: torch.Tensor | None = None,
+                      workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """This rank's fp32 share of the layer (the local experts of data["config"]): fp32 [T, H],
+    the sum over local slots before the bf16 cast; zeros for tokens with no local pair. The sum
+    of every rank's share, cast to bf16, is kernel_fn's output over all experts."""
+    args, out = _call_args(data, state, out, workspace, torch.float32)
+    _lib.call("muse_moe_forward_partial", *args)
+    return out
+
+
+def cast_bf16(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 copy of a contiguous fp32 CUDA tensor (numel a multiple of 8), on the current stream."""
+    _require_cuda(x, "x")
+    if x.dtype != torch.float32 or not x.is_contiguous() or x.numel() % 8:
+        raise _lib.MuseError(_lib.MUSE_ERR_INVALID_ARGUMENT, "cast_bf16 needs contiguous fp32, numel % 8 == 0")
+    if out is None:
+        out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+    _lib.call("muse_moe_cast_bf16", _ptr(x), _ptr(out), x.numel(), _stream(x.device))
     return out
 
 

@@ -341,3 +341,37 @@ def test_profiled_forward_matches_and_times(pkg, synth, cfg2_weights, T):
     assert torch.equal(got.view(torch.int16), ref.view(torch.int16))
     gaps = [ev[i].elapsed_time(ev[i + 1]) for i in range(4)]
     assert all(g >= 0 for g in gaps) and gaps[1] > 0 and gaps[2] > 0, gaps
+
+
+@pytest.mark.parametrize("T", [3, 40, 300])
+def test_partial_shares_sum_to_the_layer(pkg, synth, T):
+    """Expert-parallel building blocks on one GPU: the fp32 shares of three disjoint expert
+    blocks (each repacked on its own, as an expert-parallel rank would), summed and cast to bf16
+    by the library, give the single-call layer's output and the oracle's."""
+    from muse_moe_w4a16_b200 import ep, layer
+    shape = synth.MoEShape(24, 4, 256, 384, router="normal")
+    w = synth.baseline_weights(shape, seed=77, device=DEV)
+    d = to_device(synth.baseline_input(shape, T, seed=T), DEV)
+    total = None
+    for r in range(3):
+        block = ep.expert_block(24, r, 3)
+        st = layer.prepare(w, block)
+        part = layer.kernel_fn_partial(ep._with_local_range(d, block), st)
+        total = part if total is None else total + part
+    got = layer.cast_bf16(total)
+    torch.cuda.synchronize()
+    whole = pkg.kernel_fn(d, pkg.prepare(w))
+    ok, msg, err, _ = orc.compare(bits(got), bits(whole), TOL)
+    assert ok and err < 1e-3, msg
+    ok, msg, _, _ = orc.compare(bits(got), oracle_out(synth.baseline_input(shape, T, seed=T), to_numpy_weights(w)), TOL)
+    assert ok, msg
+
+
+def test_cast_bf16_rounds_to_nearest_even(pkg):
+    from muse_moe_w4a16_b200 import layer
+    x = torch.randn(4096, device=DEV) * torch.logspace(-30, 30, 4096, device=DEV)
+    x[:4] = torch.tensor([1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8, -0.0, float("inf")], device=DEV)
+    got = layer.cast_bf16(x)
+    torch.cuda.synchronize()
+    ref = orc.f32_to_bf16(x.cpu().numpy())
+    np.testing.assert_array_equal(bits(got), ref)
