@@ -192,7 +192,8 @@ int forward_impl(const void* x, const int32_t* topk_ids, const float* topk_weigh
   const int P = d.n_pairs();
   const int rows = (int)pair_rows(tokens, top_k);
   const int n_box = pick_n_box(tokens, top_k, local_count);
-  const int stages = pick_stages(n_box);
+  int b_stages = 0;
+  const int stages = pick_stages(n_box, &b_stages);
   auto mark = [&](int i) -> int { return ev ? (int)cudaEventRecord(ev[i], st) : 0; };
 
   // Small batches: the first GEMM routes in its prologue and gathers x rows itself, so neither
@@ -221,6 +222,7 @@ int forward_impl(const void* x, const int32_t* topk_ids, const float* topk_weigh
   g1.k_chunks = hidden / kChunkK;
   g1.n_box = n_box;
   g1.stages = stages;
+  g1.b_stages = b_stages;
   g1.wq = w13p;
   g1.wsf = w13_sfp;
   g1.gs = w13_gs;
@@ -323,7 +325,8 @@ extern "C" int muse_moe_launch_plan(int tokens, int top_k, int local_count, int 
   const bool inline_route = tokens * top_k <= kMaxInlinePairs && n_box <= kMaxInlineBox;
   plan[0] = tokens == 0 ? 0 : (inline_route ? 3 : 5);
   plan[1] = n_box;
-  plan[2] = pick_stages(n_box);
+  int b_stages = 0;
+  plan[2] = pick_stages(n_box, &b_stages);
   plan[3] = inline_route ? 1 : 0;
   return MUSE_OK;
 }

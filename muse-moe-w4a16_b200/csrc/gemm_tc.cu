@@ -54,9 +54,14 @@ constexpr int kMaxExperts = kMaxLocalExperts;
 // raw code value = e2m1 * 2^-126; scales held as sf * 2^60; product = e2m1 * sf * 2^-66.
 constexpr float kUnscale = 73786976294838206464.0f;  // 2^66
 
+// Two rings per pipeline: weight tiles (freed by the dequantisers as soon as they have read
+// them) and activation boxes (freed when the MMAs that read them complete), so a weight slot
+// is refilled without waiting for the tensor core.
 struct PipeCtl {
-  uint64_t full[kMaxStages];
-  uint64_t empty[kMaxStages];
+  uint64_t w_full[kMaxStages];
+  uint64_t w_empty[kMaxStages];
+  uint64_t b_full[kMaxStages];
+  uint64_t b_empty[kMaxStages];
   uint64_t a_full[kMaxABuf];
   uint64_t a_empty[kMaxABuf];
   uint64_t acc_full[2];
@@ -77,21 +82,24 @@ struct SharedCtl {
 
 // Per-launch geometry shared by all roles.
 struct Geo {
-  int S;              // stages per pipeline
+  int Sw, Sb;         // weight / activation ring depths per pipeline
   int n_box;          // token tile = MMA N
   int n_a, n_acc;     // A buffers and accumulators per pipeline
-  uint32_t b_bytes, stage_bytes;
+  uint32_t b_bytes;   // one activation slot: two 64-column boxes of n_box rows
+  uint32_t pipe_bytes;
 };
+constexpr uint32_t kWStageBytes = kTileCodeBytes + kTileScaleBytes;  // 9 KiB, 1 KiB multiple
 
-__host__ __device__ inline Geo make_geo(int pipe_cols, int n_box, int stages) {
+__host__ __device__ inline Geo make_geo(int pipe_cols, int n_box, int w_stages, int b_stages) {
   Geo g;
-  g.S = stages;
+  g.Sw = w_stages;
+  g.Sb = b_stages;
   g.n_box = n_box;
   g.n_acc = 2 * n_box <= pipe_cols / 2 ? 2 : 1;
   g.n_a = (pipe_cols - g.n_acc * n_box) / kACols;
   if (g.n_a > kMaxABuf) g.n_a = kMaxABuf;
   g.b_bytes = 2u * n_box * 128u;
-  g.stage_bytes = g.b_bytes + kTileCodeBytes + kTileScaleBytes;
+  g.pipe_bytes = w_stages * kWStageBytes + b_stages * g.b_bytes;
   return g;
 }
 
@@ -163,11 +171,14 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
   constexpr int kPipeCols = R::kPipeCols;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const Geo geo = make_geo(kPipeCols, a.n_box, a.stages);
-  const int S = geo.S, n_box = geo.n_box;
-  SharedCtl& ctl = *reinterpret_cast<SharedCtl*>(smem + (size_t)kPipes * S * geo.stage_bytes);
-  // stage s of pipeline p: [B boxes | fp4 codes | scales]
-  auto stage_ptr = [&](int p, int s) { return smem + ((size_t)p * S + s) * geo.stage_bytes; };
+  const Geo geo = make_geo(kPipeCols, a.n_box, a.stages, a.b_stages);
+  const int Sw = geo.Sw, Sb = geo.Sb, n_box = geo.n_box;
+  SharedCtl& ctl = *reinterpret_cast<SharedCtl*>(smem + (size_t)kPipes * geo.pipe_bytes);
+  // pipeline p: Sw weight slots [fp4 codes | scales], then Sb activation slots [box | box]
+  auto w_slot = [&](int p, int s) { return smem + (size_t)p * geo.pipe_bytes + (size_t)s * kWStageBytes; };
+  auto b_slot = [&](int p, int s) {
+    return smem + (size_t)p * geo.pipe_bytes + (size_t)Sw * kWStageBytes + (size_t)s * geo.b_bytes;
+  };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_local = a.n_local;
@@ -176,9 +187,13 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
   if (threadIdx.x == 0) {
     for (int p = 0; p < kPipes; ++p) {
       PipeCtl& pc = ctl.pipe[p];
-      for (int s = 0; s < S; ++s) {
-        ptx::mbar_init(&pc.full[s], 1);
-        ptx::mbar_init(&pc.empty[s], 1 + 4);  // MMA commit + 4 dequant warps
+      for (int s = 0; s < Sw; ++s) {
+        ptx::mbar_init(&pc.w_full[s], 1);
+        ptx::mbar_init(&pc.w_empty[s], 4);  // the 4 dequant warps
+      }
+      for (int s = 0; s < Sb; ++s) {
+        ptx::mbar_init(&pc.b_full[s], 1);
+        ptx::mbar_init(&pc.b_empty[s], 1);  // MMA commit
       }
       for (int b = 0; b < geo.n_a; ++b) {
         ptx::mbar_init(&pc.a_full[b], 4);
@@ -258,11 +273,13 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     // ------------------------------------------------------------------ producers
     const int p = warp;
     PipeCtl& pc = ctl.pipe[p];
-    if (lane == 0) {
+    {
+      // The whole warp walks the loop (warp-uniform values stay in uniform registers); the
+      // elected leader issues the copies.
+      const bool leader = ptx::elect_one();
       bool ok = true;
-      int stage = 0;
-      uint32_t phase = 0;
-      int issued = 0;
+      Ring ws, bs;
+      int w_issued = 0, b_issued = 0;
       int jm = 0;
       for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
         const int kc0 = first_chunk(p, jm);
@@ -270,45 +287,67 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
         const Item t = decode_item(ctl, offs, blockIdx.x + j * G, n_local, n_box);
         const size_t tile0 = ((size_t)t.e * a.m_tiles + t.m) * kcn;
         for (int kc = kc0; kc < kcn; kc += kPipes) {
-          if (!ptx::mbar_wait_sleep(&pc.empty[stage], phase ^ 1)) { ok = false; break; }
-          uint8_t* sp = stage_ptr(p, stage);
+          if (!__all_sync(0xffffffffu, ptx::mbar_wait_sleep(&pc.w_empty[ws.slot], ws.phase ^ 1))) {
+            ok = false;
+            break;
+          }
+          uint8_t* wp = w_slot(p, ws.slot);
+          if (leader) {
+            ptx::mbar_arrive_expect_tx(&pc.w_full[ws.slot], kWStageBytes);
+            ptx::bulk_g2s(wp, a.wq + (tile0 + kc) * kTileCodeBytes, kTileCodeBytes, &pc.w_full[ws.slot]);
+            ptx::bulk_g2s(wp + kTileCodeBytes, a.wsf + (tile0 + kc) * kTileScaleBytes, kTileScaleBytes,
+                          &pc.w_full[ws.slot]);
+          }
+          ++w_issued;
+          ws.next(Sw);
+          if (!__all_sync(0xffffffffu, ptx::mbar_wait_sleep(&pc.b_empty[bs.slot], bs.phase ^ 1))) {
+            ok = false;
+            break;
+          }
+          uint8_t* bp = b_slot(p, bs.slot);
+          uint64_t* bb = &pc.b_full[bs.slot];
           if (a.route_inline) {
             // Activation rows straight from x[token], four rows per gather; only the groups that
             // hold the tile's pairs are loaded (the MMA columns of the rest are never read).
             const int groups = (t.nvalid + 3) >> 2;
-            ptx::mbar_arrive_expect_tx(&pc.full[stage], kTileCodeBytes + kTileScaleBytes + groups * 1024);
             const int* tok = ctl.order + t.row0;
             const int last = t.nvalid - 1;
-            for (int g4 = 0; g4 < groups; ++g4) {
-              const int i = 4 * g4;
-              const int r0 = tok[i], r1 = tok[min(i + 1, last)], r2 = tok[min(i + 2, last)],
-                        r3 = tok[min(i + 3, last)];
-              ptx::tma_gather4_2d(sp + i * 128, &tmap_x, kc * kChunkK, r0, r1, r2, r3, &pc.full[stage]);
-              ptx::tma_gather4_2d(sp + (n_box + i) * 128, &tmap_x, kc * kChunkK + 64, r0, r1, r2, r3,
-                                  &pc.full[stage]);
+            if (leader) {
+              ptx::mbar_arrive_expect_tx(bb, groups * 1024);
+              for (int g4 = 0; g4 < groups; ++g4) {
+                const int i = 4 * g4;
+                const int r0 = tok[i], r1 = tok[min(i + 1, last)], r2 = tok[min(i + 2, last)],
+                          r3 = tok[min(i + 3, last)];
+                ptx::tma_gather4_2d(bp + i * 128, &tmap_x, kc * kChunkK, r0, r1, r2, r3, bb);
+                ptx::tma_gather4_2d(bp + (n_box + i) * 128, &tmap_x, kc * kChunkK + 64, r0, r1, r2, r3, bb);
+              }
             }
-          } else {
-            ptx::mbar_arrive_expect_tx(&pc.full[stage], geo.stage_bytes);
-            ptx::tma_load_2d(sp, &tmap_b, kc * kChunkK, t.row0, &pc.full[stage]);
-            ptx::tma_load_2d(sp + n_box * 128, &tmap_b, kc * kChunkK + 64, t.row0, &pc.full[stage]);
+          } else if (leader) {
+            ptx::mbar_arrive_expect_tx(bb, geo.b_bytes);
+            ptx::tma_load_2d(bp, &tmap_b, kc * kChunkK, t.row0, bb);
+            ptx::tma_load_2d(bp + n_box * 128, &tmap_b, kc * kChunkK + 64, t.row0, bb);
           }
-          ptx::bulk_g2s(sp + geo.b_bytes, a.wq + (tile0 + kc) * kTileCodeBytes, kTileCodeBytes, &pc.full[stage]);
-          ptx::bulk_g2s(sp + geo.b_bytes + kTileCodeBytes, a.wsf + (tile0 + kc) * kTileScaleBytes,
-                        kTileScaleBytes, &pc.full[stage]);
-          ++issued;
-          if (++stage == S) { stage = 0; phase ^= 1; }
+          ++b_issued;
+          bs.next(Sb);
         }
       }
       if (!ok) {
-        record_error(a.error_flag, 1);
+        if (leader) record_error(a.error_flag, 1);
         // let copies already in flight land before the CTA can exit: walk back over the last
-        // min(issued, S) stages
-        int s = stage;
-        uint32_t ph = phase;
-        for (int i = 0; i < issued && i < S; ++i) {
-          if (s == 0) { s = S; ph ^= 1u; }
+        // min(issued, depth) slots of each ring
+        int s = ws.slot;
+        uint32_t ph = ws.phase;
+        for (int i = 0; i < w_issued && i < Sw; ++i) {
+          if (s == 0) { s = Sw; ph ^= 1u; }
           --s;
-          ptx::mbar_wait(&pc.full[s], ph);
+          ptx::mbar_wait(&pc.w_full[s], ph);
+        }
+        s = bs.slot;
+        ph = bs.phase;
+        for (int i = 0; i < b_issued && i < Sb; ++i) {
+          if (s == 0) { s = Sb; ph ^= 1u; }
+          --s;
+          ptx::mbar_wait(&pc.b_full[s], ph);
         }
       }
     }
@@ -316,50 +355,64 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     // ------------------------------------------------------------------ MMA issuers
     const int p = warp - kMmaWarp0;
     PipeCtl& pc = ctl.pipe[p];
-    if (lane == 0) {
+    {
+      // The whole warp walks the loop; the elected leader issues the MMAs and the commits that
+      // track them (a commit covers the MMAs of its own thread).
+      const bool leader = ptx::elect_one();
       bool ok = true;
       const uint32_t idesc = ptx::idesc_bf16_f32(kTileM, n_box);
       const uint32_t col0 = tbase + p * kPipeCols;
       const uint32_t acc_col0 = col0 + geo.n_a * kACols;
-      // The dequantisers arrive on a_full only after observing the stage's full barrier, so
-      // a_full alone orders the MMAs after both the A buffer and the stage's B boxes.
       Ring st, ar, accr;
-      const uint64_t desc_first = ptx::smem_desc_k_sw128(ptx::smem_u32(stage_ptr(p, 0)), 1024);
-      const uint32_t stage_step = geo.stage_bytes >> 4;       // descriptor units (16 B)
-      const uint32_t atom_step = (uint32_t)(n_box * 128) >> 4;  // second 64-K box of a stage
+      const uint64_t desc_first = ptx::smem_desc_k_sw128(ptx::smem_u32(b_slot(p, 0)), 1024);
+      const uint32_t stage_step = geo.b_bytes >> 4;              // descriptor units (16 B)
+      const uint32_t atom_step = (uint32_t)(n_box * 128) >> 4;  // second 64-K box of a slot
       uint64_t desc_stage = desc_first;
       int jm = 0;
       for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
         const int kc0 = first_chunk(p, jm);
         if (kc0 >= kcn) continue;
         const int acc = accr.slot;
-        if (!ptx::mbar_wait_sleep(&pc.acc_empty[acc], accr.phase ^ 1)) { ok = false; break; }
+        if (!__all_sync(0xffffffffu, ptx::mbar_wait_sleep(&pc.acc_empty[acc], accr.phase ^ 1))) {
+          ok = false;
+          break;
+        }
         ptx::tc_fence_after();
         const uint32_t d_tmem = acc_col0 + acc * n_box;
         for (int kc = kc0; kc < kcn; kc += kPipes) {
           const int s = st.slot;
           const int ab = ar.slot;
-          if (!ptx::mbar_wait(&pc.a_full[ab], ar.phase)) { ok = false; break; }
+          const bool ready = ptx::mbar_wait_sleep(&pc.a_full[ab], ar.phase) &&
+                             ptx::mbar_wait_sleep(&pc.b_full[s], st.phase);
+          if (!__all_sync(0xffffffffu, ready)) {
+            ok = false;
+            break;
+          }
           ptx::tc_fence_after();
           const uint32_t a_tmem = col0 + ab * kACols;
+          if (leader) {
 #pragma unroll
-          for (int kk = 0; kk < kChunkK / 16; ++kk) {
-            const uint64_t bdesc = desc_stage + (uint64_t)((kk >> 2) * atom_step + (kk & 3) * 2);
-            ptx::mma_bf16_ts(d_tmem, a_tmem + kk * 8, bdesc, idesc, (kc != kc0) | (kk != 0));
+            for (int kk = 0; kk < kChunkK / 16; ++kk) {
+              const uint64_t bdesc = desc_stage + (uint64_t)((kk >> 2) * atom_step + (kk & 3) * 2);
+              ptx::mma_bf16_ts(d_tmem, a_tmem + kk * 8, bdesc, idesc, (kc != kc0) | (kk != 0));
+            }
+            ptx::mma_commit(&pc.b_empty[s]);
+            ptx::mma_commit(&pc.a_empty[ab]);
           }
-          ptx::mma_commit(&pc.empty[s]);
-          ptx::mma_commit(&pc.a_empty[ab]);
+          __syncwarp();
           ar.next(geo.n_a);
-          st.next(S);
+          st.next(Sb);
           desc_stage = st.slot == 0 ? desc_first : desc_stage + stage_step;
         }
         if (!ok) break;
-        ptx::mma_commit(&pc.acc_full[acc]);
+        if (leader) ptx::mma_commit(&pc.acc_full[acc]);
+        __syncwarp();
         accr.next(geo.n_acc);
       }
-      if (!ok) record_error(a.error_flag, 2);
+      if (!ok && leader) record_error(a.error_flag, 2);
       // all issued MMAs complete before tensor memory is released
-      ptx::mma_commit(&pc.drain);
+      if (leader) ptx::mma_commit(&pc.drain);
+      __syncwarp();
       ptx::mbar_wait(&pc.drain, 0);
     }
   } else if (warp < kDeqWarp0) {
@@ -398,15 +451,16 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
 #pragma unroll
             for (int c = 0; c < 16; ++c) acc[c] += __uint_as_float(v[c]);
           }
+          const int ncols = min(16, t.nvalid - cb * 16);  // warp-uniform
 #pragma unroll
           for (int col = 0; col < 16; ++col) {
+            if (col >= ncols) break;
             const float mine = acc[col] * gsc;
             const float other = __shfl_xor_sync(0xffffffffu, mine, 16);
-            const int n = cb * 16 + col;
-            if (lane < 16 && n < t.nvalid) {
+            if (lane < 16) {
               const float act = mine / (1.0f + __expf(-mine)) * other;
               const __nv_bfloat16 hb = __float2bfloat16_rn(act);
-              a.inter[(size_t)(t.row0 + n) * a.ld_out + jj] = *reinterpret_cast<const uint16_t*>(&hb);
+              a.inter[(size_t)(t.row0 + cb * 16 + col) * a.ld_out + jj] = *reinterpret_cast<const uint16_t*>(&hb);
             }
           }
         }
@@ -462,20 +516,31 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     Ring st, ar;
     int jm = 0;
     for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
-      for (int kc = first_chunk(p, jm); kc < kcn; kc += kPipes, st.next(S), ar.next(geo.n_a)) {
+      for (int kc = first_chunk(p, jm); kc < kcn; kc += kPipes, st.next(Sw), ar.next(geo.n_a)) {
         const int s = st.slot;
         const int ab = ar.slot;
-        if (!ptx::mbar_wait(&pc.full[s], st.phase) || !ptx::mbar_wait(&pc.a_empty[ab], ar.phase ^ 1)) {
+        if (!ptx::mbar_wait_sleep(&pc.w_full[s], st.phase)) {
           ok = false;
           break;
         }
-        const uint8_t* sp = stage_ptr(p, s) + geo.b_bytes;
-        const uint8_t* arow = sp + row * kRowCodeBytes;
-        const uint2 sfw = *reinterpret_cast<const uint2*>(sp + kTileCodeBytes + row * kRowScaleBytes);
+        // read this row's 64 code bytes and 8 scale bytes, then hand the weight slot back to
+        // the producer before doing any arithmetic
+        const uint8_t* wp = w_slot(p, s);
+        const uint8_t* arow = wp + row * kRowCodeBytes;
+        uint4 cw[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) cw[c] = *reinterpret_cast<const uint4*>(arow + 16 * code_slot(row, c));
+        const uint2 sfw = *reinterpret_cast<const uint2*>(wp + kTileCodeBytes + row * kRowScaleBytes);
+        __syncwarp();
+        if (lane == 0) ptx::mbar_arrive(&pc.w_empty[s]);
+        if (!ptx::mbar_wait_sleep(&pc.a_empty[ab], ar.phase ^ 1)) {
+          ok = false;
+          break;
+        }
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
-          const uint4 c0 = *reinterpret_cast<const uint4*>(arow + 16 * code_slot(row, 2 * half));
-          const uint4 c1 = *reinterpret_cast<const uint4*>(arow + 16 * code_slot(row, 2 * half + 1));
+          const uint4 c0 = cw[2 * half];
+          const uint4 c1 = cw[2 * half + 1];
           const uint32_t sw = half ? sfw.y : sfw.x;  // the 4 scale bytes of these 64 elements
           const uint32_t sc[4] = {ctl.scale_lut[__byte_perm(sw, 0, 0x4440)],
                                   ctl.scale_lut[__byte_perm(sw, 0, 0x4441)],
@@ -495,10 +560,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
         ptx::tmem_wait_st();
         ptx::tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          ptx::mbar_arrive(&pc.a_full[ab]);
-          ptx::mbar_arrive(&pc.empty[s]);
-        }
+        if (lane == 0) ptx::mbar_arrive(&pc.a_full[ab]);
       }
     }
     if (!ok && lane == 0) record_error(a.error_flag, 4);
@@ -544,18 +606,29 @@ int pick_pipes(int n_box) { return n_box <= 16 ? 3 : 2; }
 
 int pipe_cols(int pipes) { return pipes == 3 ? Variant<3>::kPipeCols : Variant<2>::kPipeCols; }
 
-size_t gemm_smem_bytes(int n_box, int stages) {
-  const int P = pick_pipes(n_box);
-  const Geo g = make_geo(pipe_cols(P), n_box, stages);
-  return 1024 + (size_t)P * stages * g.stage_bytes + sizeof(SharedCtl);
+size_t gemm_smem_bytes(int n_box, int w_stages, int b_stages) {
+  const Geo g = make_geo(pipe_cols(pick_pipes(n_box)), n_box, w_stages, b_stages);
+  return 1024 + (size_t)pick_pipes(n_box) * g.pipe_bytes + sizeof(SharedCtl);
 }
 
-int pick_stages(int n_box) {
+// Ring depths for a token tile: the deepest weight ring that fits 220 KB with one activation
+// slot more than weight slots (an activation slot lives until its MMAs complete, a weight slot
+// only until it has been read), else equal depths.
+int pick_stages(int n_box, int* b_stages) {
   const int P = pick_pipes(n_box);
-  const Geo g = make_geo(pipe_cols(P), n_box, 1);
-  const size_t budget = 220u * 1024u - sizeof(SharedCtl) - 1024;
-  int s = (int)(budget / (P * g.stage_bytes));
-  return s < kMaxStages ? s : kMaxStages;
+  const Geo g = make_geo(pipe_cols(P), n_box, 1, 1);
+  const size_t budget = (220u * 1024u - sizeof(SharedCtl) - 1024) / P;
+  for (int sw = kMaxStages; sw >= 2; --sw) {
+    for (int extra = 1; extra >= 0; --extra) {
+      const int sb = sw + extra;
+      if (sb <= kMaxStages && sw * (size_t)kWStageBytes + sb * (size_t)g.b_bytes <= budget) {
+        *b_stages = sb;
+        return sw;
+      }
+    }
+  }
+  *b_stages = 2;
+  return 2;
 }
 
 int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, const GemmArgs& args,
@@ -575,14 +648,16 @@ int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, con
     if (e != cudaSuccess) return e;
     g_attr_set[dev] = true;
   }
-  if (args.stages < 2) return MUSE_ERR_UNSUPPORTED_SHAPE;
-  const Geo g = make_geo(pipe_cols(pick_pipes(args.n_box)), args.n_box, args.stages);
+  if (args.stages < 2 || args.b_stages < 2 || args.stages > kMaxStages || args.b_stages > kMaxStages)
+    return MUSE_ERR_UNSUPPORTED_SHAPE;
+  const Geo g = make_geo(pipe_cols(pick_pipes(args.n_box)), args.n_box, args.stages, args.b_stages);
   if (g.n_a < 2) return MUSE_ERR_UNSUPPORTED_SHAPE;
   if (args.route_inline &&
       (args.n_pairs > kMaxInlinePairs || args.n_box > kMaxInlineBox || !args.ids || !args.pair_order ||
        !args.pair_row))
     return MUSE_ERR_UNSUPPORTED_SHAPE;
-  const size_t smem = gemm_smem_bytes(args.n_box, args.stages);
+  const size_t smem = gemm_smem_bytes(args.n_box, args.stages, args.b_stages);
+  if (smem > 227u * 1024u) return MUSE_ERR_UNSUPPORTED_SHAPE;
   if (pick_pipes(args.n_box) == 3)
     expert_gemm_tc<3><<<g_num_sms[dev], Variant<3>::kThreads, smem, stream>>>(tmap_b, tmap_x, args);
   else

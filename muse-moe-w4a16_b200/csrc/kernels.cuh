@@ -44,7 +44,8 @@ struct GemmArgs {
   int m_tiles;             // weight rows per expert / 128
   int k_chunks;            // K / 128
   int n_box;               // token tile = MMA N (16, 32, 64 or 128)
-  int stages;              // shared-memory ring depth
+  int stages;              // weight-tile ring depth (shared memory)
+  int b_stages;            // activation-box ring depth (shared memory)
   const uint8_t* wq;       // prepared codes
   const uint8_t* wsf;      // prepared scales
   const float* gs;         // [n_local] global scales
@@ -77,8 +78,9 @@ int launch_route(const int32_t* ids, int tokens, int top_k, int local_start, int
 int launch_gather(const uint16_t* x, const int32_t* offsets, const int32_t* pair_order, int n_local,
                   int top_k, int max_rows, int hidden, uint16_t* xs, cudaStream_t stream);
 
-size_t gemm_smem_bytes(int n_box, int stages);
-int pick_stages(int n_box);
+size_t gemm_smem_bytes(int n_box, int w_stages, int b_stages);
+// Weight-ring depth for a token tile; *b_stages receives the activation-ring depth.
+int pick_stages(int n_box, int* b_stages);
 int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, const GemmArgs& args,
                        cudaStream_t stream);
 

@@ -219,5 +219,17 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
 
 __device__ __forceinline__ uint32_t rotl(uint32_t x, int n) { return __funnelshift_l(x, x, n); }
 
+// One lane of the (fully active) warp is elected; the others get false. The same lane every
+// time for a given warp state, so a role can decide its leader once.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\t"
+      "elect.sync _|P, 0xffffffff;\n\t"
+      "selp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 }  // namespace ptx
 }  // namespace muse
