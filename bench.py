@@ -392,15 +392,20 @@ def run_muse(args, world, rank, local):
         pre, k1, k2, comb = stage_us[t]
         plan = _lib.launch_plan(t, shape.top_k, len(experts), shape.hidden, shape.inter)
         launches_per_step += plan["launches"] + (1 if world > 1 else 0)   # + the bf16 cast
+        fused = plan["fused"]
         gbs = b / (us * 1e-6) / 1e9
-        g1_bytes += b1
+        # the dominant kernel: the single layer kernel of a fused call, else GEMM1
+        g1_bytes += b if fused else b1
         g1_time += k1
         row = {"T": t, "us": round(us, 3), "bytes": b, "flops": f, "GBps": round(gbs, 1),
                "hbm_frac": round(gbs / (pk["hbm_gbs"] * world), 4),
                "roofline_us": round(max(b / (pk["hbm_gbs"] * world) / 1e3,
                                         f / (pk["bf16_tflops"] * world) / 1e6), 3),
-               "launches": plan["launches"], "n_box": plan["n_box"], "route_inline": plan["route_inline"]}
-        if world == 1:   # per-kernel event times (single-GPU calls only)
+               "launches": plan["launches"], "n_box": plan["n_box"], "path": plan["path"]}
+        if world == 1 and fused:   # per-kernel event times (single-GPU calls only)
+            row.update({"kernels_us": {"layer": round(k1, 3)},
+                        "layer_kernel_GBps": round(b / (k1 * 1e-6) / 1e9, 1)})
+        elif world == 1:
             row.update({"kernels_us": {"route_gather": round(pre, 3), "gemm1": round(k1, 3),
                                        "gemm2": round(k2, 3), "combine": round(comb, 3)},
                         "gemm1_GBps": round(b1 / (k1 * 1e-6) / 1e9, 1),
@@ -408,8 +413,9 @@ def run_muse(args, world, rank, local):
         per_rows.append(row)
     if world == 1:
         achieved = g1_bytes / (g1_time * 1e-6) / 1e9
-        roof_kernel = ("expert_gemm_tc, GEMM1 launch (w13 + SiLU*up): algorithmic bytes per "
-                       "launch / mean CUDA-event duration, summed over the token sweep")
+        roof_kernel = ("expert_gemm_tc launch of each call's dominant kernel (the single fused "
+                       "layer kernel for decode batches, else GEMM1): algorithmic bytes per launch / "
+                       "mean CUDA-event duration, summed over the token sweep")
         roof_peak = pk["hbm_gbs"]
     else:
         # whole expert-parallel call: every rank's algorithmic bytes over the slowest rank's

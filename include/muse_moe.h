@@ -59,9 +59,10 @@ int muse_moe_workspace_size(int tokens, int top_k, int local_count, int hidden, 
 
 /*
  * Byte offsets of the scratch buffers inside the workspace, for inspection by tests:
- * offsets[0..7] = expert_offsets, pair_order, pair_row, xs (bf16 [T*K, H] gathered hidden
+ * offsets[0..8] = expert_offsets, pair_order, pair_row, xs (bf16 [T*K, H] gathered hidden
  * states), inter (bf16 [T*K, I]), ypart (fp32 [T*K, H]), ssq (fp32 [T*K, H/32]: the sum of
- * squares of each 32-column slice of a ypart row), total bytes.
+ * squares of each 32-column slice of a ypart row), sync (int32 token-tile counters of the
+ * single-launch path, zeroed by each call), total bytes.
  * Rows of xs / inter / ypart / ssq are in pair_order order.
  */
 int muse_moe_workspace_offsets(int tokens, int top_k, int local_count, int hidden, int inter,
@@ -159,9 +160,12 @@ int muse_moe_forward_profiled(const void* x, const int32_t* topk_ids, const floa
 
 /*
  * The launch plan of one muse_moe_forward call for these shapes (host only, no device work):
- *   plan[0] kernels launched (3 when the first GEMM routes in its prologue, else 5; 0 if T = 0)
+ *   plan[0] kernels launched (1, 3 or 5, by plan[3]; 0 if T = 0)
  *   plan[1] token tile (the MMA's N), plan[2] pipeline stages,
- *   plan[3] 1 when routing and the activation gather run inside the first GEMM.
+ *   plan[3] 2: the whole layer in one cooperative launch after a memset of its counters
+ *              (T*K <= 128 and token tile <= 32); 1: GEMM1 routes and gathers x in its own
+ *              prologue, then GEMM2 and the combine (T*K <= 1024, token tile <= 32);
+ *           0: route, gather, GEMM1, GEMM2, combine.
  * No counterpart in the reference; a diagnostic for benchmarks and tests.
  */
 int muse_moe_launch_plan(int tokens, int top_k, int local_count, int hidden, int inter,

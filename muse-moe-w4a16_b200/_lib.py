@@ -98,9 +98,9 @@ def call(name: str, *args) -> None:
 
 def workspace_offsets(tokens: int, top_k: int, local_count: int, hidden: int, inter: int) -> dict:
     """Byte offsets of the scratch buffers inside the workspace (include/muse_moe.h)."""
-    arr = (ctypes.c_size_t * 8)()
+    arr = (ctypes.c_size_t * 9)()
     call("muse_moe_workspace_offsets", tokens, top_k, local_count, hidden, inter, arr)
-    names = ("offsets", "pair_order", "pair_row", "xs", "inter", "ypart", "ssq", "total")
+    names = ("offsets", "pair_order", "pair_row", "xs", "inter", "ypart", "ssq", "sync", "total")
     return dict(zip(names, (int(v) for v in arr)))
 
 
@@ -121,4 +121,5 @@ def launch_plan(tokens: int, top_k: int, local_count: int, hidden: int, inter: i
     """Kernels, token tile, stages and routing mode of one forward call (include/muse_moe.h)."""
     arr = (ctypes.c_int * 4)()
     call("muse_moe_launch_plan", tokens, top_k, local_count, hidden, inter, arr)
-    return {"launches": arr[0], "n_box": arr[1], "stages": arr[2], "route_inline": bool(arr[3])}
+    return {"launches": arr[0], "n_box": arr[1], "stages": arr[2], "path": int(arr[3]),
+            "fused": arr[3] == 2, "route_inline": arr[3] >= 1}

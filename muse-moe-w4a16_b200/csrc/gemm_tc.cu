@@ -72,12 +72,15 @@ struct PipeCtl {
 struct SharedCtl {
   PipeCtl pipe[kMaxPipes];
   uint32_t tmem_base;
-  int item_warp_sum[8];              // items of experts [32w, 32w + 32)
-  int item_prefix[kMaxExperts + 1];  // cumulative items per expert
+  int tile_warp_sum[8];              // token tiles of experts [32w, 32w + 32)
+  int tile_prefix[kMaxExperts + 1];  // cumulative token tiles per expert
   int ntiles[kMaxExperts];           // token tiles per expert
   uint32_t scale_lut[256];           // e4m3 byte -> bf16x2 (sf * 2^60, sf * 2^60)
   int offs[kMaxExperts + 1];         // route_inline: expert ranges of the pair rows
   int order[kMaxInlinePairs];        // route_inline: token of each expert-grouped pair row
+  uint8_t slot_of_row[kMaxInlinePairs];  // route_inline: top-k slot of each pair row
+  int c_row[kMaxTopK], c_key[kMaxTopK], c_order[kMaxTopK], c_n;  // combine of one token
+  float c_coef[kMaxTopK];
 };
 
 // Per-launch geometry shared by all roles.
@@ -103,8 +106,10 @@ __host__ __device__ inline Geo make_geo(int pipe_cols, int n_box, int w_stages, 
   return g;
 }
 
+// One work item: phase (GEMM), expert, 128-row weight tile m, token tile n (rows row0 ..
+// row0 + nvalid of the expert-grouped pairs), and the token tile's index over all experts.
 struct Item {
-  int e, m, n, row0, nvalid;
+  int ph, e, m, n, row0, nvalid, tile;
 };
 
 // Position in a ring of `size` slots: slot index and the parity of the slot's current use.
@@ -117,19 +122,25 @@ struct Ring {
   }
 };
 
-__device__ __forceinline__ Item decode_item(const SharedCtl& c, const int32_t* offsets, int it,
-                                            int n_local, int n_box) {
-  int lo = 0, hi = n_local;  // largest e with prefix[e] <= it (a non-empty expert)
+// Items are numbered phase by phase: phase 0 has tiles x ph[0].m_tiles items (n0), then phase
+// 1. Inside a phase, expert e owns items [tile_prefix[e] * m_tiles, tile_prefix[e + 1] * m_tiles).
+__device__ __forceinline__ Item decode_item(const SharedCtl& c, const int32_t* offsets, int it, int n0,
+                                            int n_local, int n_box, int mt0, int mt1) {
+  Item r;
+  r.ph = it >= n0;
+  if (r.ph) it -= n0;
+  const int mt = r.ph ? mt1 : mt0;
+  int lo = 0, hi = n_local;  // largest e with tile_prefix[e] * mt <= it (a non-empty expert)
   while (hi - lo > 1) {
     const int mid = (lo + hi) >> 1;
-    if (c.item_prefix[mid] <= it) lo = mid; else hi = mid;
+    if (c.tile_prefix[mid] * mt <= it) lo = mid; else hi = mid;
   }
-  Item r;
   r.e = lo;
-  const int local = it - c.item_prefix[lo];
+  const int local = it - c.tile_prefix[lo] * mt;
   const int nt = c.ntiles[lo];
   r.m = local / nt;
   r.n = local - r.m * nt;
+  r.tile = c.tile_prefix[lo] + r.n;
   const int begin = offsets[lo], cnt = offsets[lo + 1] - begin;
   r.row0 = begin + r.n * n_box;
   r.nvalid = min(n_box, cnt - r.n * n_box);
@@ -161,10 +172,92 @@ __device__ __forceinline__ void record_error(int* flag, int code) {
   if (flag) atomicExch(flag, code);
 }
 
+// The layer's combine for the tokens of this CTA (fused launches): out[t] = sum over t's local
+// slots, in ascending expert order, of topk_weight * rsqrt(mean(ypart^2) + eps) * ypart, fp32,
+// then bf16 (or fp32 for an expert-parallel share). Rows are waited for through the GEMM2
+// tile counters. Restates reference.py:88-90,106-107 like combine.cu.
+__device__ __forceinline__ void combine_tokens(SharedCtl& ctl, const GemmArgs& a, int n_local, int n_box) {
+  const int K = a.top_k, H = a.hidden, parts = H >> 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int total_rows = ctl.offs[n_local];
+  for (int t = blockIdx.x; t < a.tokens; t += gridDim.x) {
+    if (threadIdx.x < K) ctl.c_row[threadIdx.x] = -1;
+    __syncthreads();
+    for (int r = threadIdx.x; r < total_rows; r += blockDim.x)
+      if (ctl.order[r] == t) ctl.c_row[ctl.slot_of_row[r]] = r;
+    __syncthreads();
+    if (warp < K) {
+      const int sl = warp;
+      const int r = ctl.c_row[sl];
+      float coef = 0.f;
+      if (r >= 0) {
+        int lo = 0, hi = n_local;  // expert of row r: largest e with offs[e] <= r
+        while (hi - lo > 1) {
+          const int mid = (lo + hi) >> 1;
+          if (ctl.offs[mid] <= r) lo = mid; else hi = mid;
+        }
+        const int tile = ctl.tile_prefix[lo] + (r - ctl.offs[lo]) / n_box;
+        const bool ready = __all_sync(0xffffffffu, lane == 0 ? ptx::wait_counter(a.ph[1].signal + tile,
+                                                                                 a.combine_target)
+                                                             : true);
+        if (!ready && lane == 0) record_error(a.error_flag, 5);
+        float sum = 0.f;
+        for (int j = lane; j < parts; j += 32) sum += __ldcg(a.ssq + (size_t)r * parts + j);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        coef = a.topk_weights[t * K + sl] * rsqrtf(sum / (float)H + kPostNormEps);
+      }
+      if (lane == 0) {
+        ctl.c_coef[sl] = coef;
+        ctl.c_key[sl] = a.ids[t * K + sl];
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {  // local slots in ascending expert id
+      int n = 0;
+      for (int sl = 0; sl < K; ++sl) {
+        if (ctl.c_row[sl] < 0) continue;
+        int j = n++;
+        while (j > 0 && ctl.c_key[ctl.c_order[j - 1]] > ctl.c_key[sl]) {
+          ctl.c_order[j] = ctl.c_order[j - 1];
+          --j;
+        }
+        ctl.c_order[j] = sl;
+      }
+      ctl.c_n = n;
+    }
+    __syncthreads();
+    const int n = ctl.c_n;
+    for (int h4 = threadIdx.x; h4 * 4 < H; h4 += blockDim.x) {
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int j = 0; j < n; ++j) {
+        const int sl = ctl.c_order[j];
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(a.ypart + (size_t)ctl.c_row[sl] * H) + h4);
+        const float c = ctl.c_coef[sl];
+        acc.x = fmaf(c, v.x, acc.x);
+        acc.y = fmaf(c, v.y, acc.y);
+        acc.z = fmaf(c, v.z, acc.z);
+        acc.w = fmaf(c, v.w, acc.w);
+      }
+      if (a.out_f32) {
+        reinterpret_cast<float4*>(static_cast<float*>(a.out) + (size_t)t * H)[h4] = acc;
+      } else {
+        __nv_bfloat162 lo2 = __floats2bfloat162_rn(acc.x, acc.y);
+        __nv_bfloat162 hi2 = __floats2bfloat162_rn(acc.z, acc.w);
+        uint2 packed;
+        packed.x = *reinterpret_cast<uint32_t*>(&lo2);
+        packed.y = *reinterpret_cast<uint32_t*>(&hi2);
+        reinterpret_cast<uint2*>(static_cast<uint16_t*>(a.out) + (size_t)t * H)[h4] = packed;
+      }
+    }
+    __syncthreads();
+  }
+}
+
 template <int P>
 __global__ void __launch_bounds__(Roles<P>::kThreads, 1)
 expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_x,
-               const GemmArgs a) {
+               const __grid_constant__ CUtensorMap tmap_b2, const GemmArgs a) {
   using R = Roles<P>;
   constexpr int kPipes = P;
   constexpr int kMmaWarp0 = R::kMmaWarp0, kEpiWarp0 = R::kEpiWarp0, kDeqWarp0 = R::kDeqWarp0;
@@ -207,7 +300,10 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     }
     ptx::fence_barrier_init();
   }
-  if (warp < kPipes && lane == 0) ptx::prefetch_tensormap(a.route_inline ? &tmap_x : &tmap_b);
+  if (warp < kPipes && lane == 0) {
+    ptx::prefetch_tensormap(a.route_inline ? &tmap_x : &tmap_b);
+    if (a.n_phases > 1) ptx::prefetch_tensormap(&tmap_b2);
+  }
   // Expert ranges: from the route kernel, or (small batches) computed here by every CTA, with
   // the stage buffers as scratch -- nothing is copied into them before the prologue ends.
   const int32_t* offs = a.offsets;
@@ -220,25 +316,25 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     }
     offs = ctl.offs;
   }
-  int incl = 0;  // items of experts [32 * warp, threadIdx.x], threads < 256
+  int incl = 0;  // token tiles of experts [32 * warp, threadIdx.x], threads < 256
   if (threadIdx.x < 256) {
     const float f = e4m3_to_float(threadIdx.x) * 1152921504606846976.0f;  // * 2^60
     const __nv_bfloat16 h = __float2bfloat16_rn(f);
     const uint32_t u = *reinterpret_cast<const uint16_t*>(&h);
     ctl.scale_lut[threadIdx.x] = u | (u << 16);
-    // items per expert, warp-inclusive scan (completed across warps below)
+    // token tiles per expert, warp-inclusive scan (completed across warps below)
     const int e = threadIdx.x;
     int cnt = 0;
     if (e < n_local) cnt = offs[e + 1] - offs[e];
     const int nt = (cnt + n_box - 1) / n_box;
     if (e < n_local) ctl.ntiles[e] = nt;
-    incl = nt * a.m_tiles;
+    incl = nt;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
       const int o = __shfl_up_sync(0xffffffffu, incl, d);
       if (lane >= d) incl += o;
     }
-    if (lane == 31) ctl.item_warp_sum[warp] = incl;
+    if (lane == 31) ctl.tile_warp_sum[warp] = incl;
   }
   if (warp == kMmaWarp0) {
     ptx::tmem_alloc(&ctl.tmem_base, kTmemCols);
@@ -247,27 +343,40 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
-  if (a.route_inline) {  // pair index -> token (CTA 0 has published the pair indices above)
-    for (int i = threadIdx.x; i < a.n_pairs; i += R::kThreads)
-      if (ctl.order[i] >= 0) ctl.order[i] /= a.top_k;
+  if (a.route_inline) {  // pair index -> token and slot (CTA 0 has published the pair indices)
+    for (int i = threadIdx.x; i < a.n_pairs; i += R::kThreads) {
+      const int pr = ctl.order[i];
+      if (pr >= 0) {
+        ctl.order[i] = pr / a.top_k;
+        ctl.slot_of_row[i] = (uint8_t)(pr - ctl.order[i] * a.top_k);
+      }
+    }
   }
   if (threadIdx.x < 256) {  // complete the scan across the 8 warps
     int before = 0;
-    for (int w = 0; w < warp; ++w) before += ctl.item_warp_sum[w];
-    ctl.item_prefix[threadIdx.x + 1] = before + incl;
-    if (threadIdx.x == 0) ctl.item_prefix[0] = 0;
+    for (int w = 0; w < warp; ++w) before += ctl.tile_warp_sum[w];
+    ctl.tile_prefix[threadIdx.x + 1] = before + incl;
+    if (threadIdx.x == 0) ctl.tile_prefix[0] = 0;
   }
   __syncthreads();
 
   const uint32_t tbase = ctl.tmem_base;
-  const int total = ctl.item_prefix[n_local];
+  const int tiles = ctl.tile_prefix[n_local];
+  const int mt0 = a.ph[0].m_tiles, mt1 = a.n_phases > 1 ? a.ph[1].m_tiles : 0;
+  const int n0 = tiles * mt0;                       // items of phase 0
+  const int total = n0 + tiles * mt1;               // all items of this launch
   const int G = gridDim.x;
-  const int kcn = a.k_chunks;
-  // Tile j of this CTA is item blockIdx.x + j * G. Its K chunks are split over the pipelines
-  // (split-K): pipeline p takes the chunks kc with (kc + j) % P == p, into its own accumulator;
-  // the epilogue sums the partial accumulators. Rotating the assignment with j balances the
-  // pipelines when P does not divide the chunk count.
-  auto first_chunk = [&](int p, int jm) { return (p - jm + kPipes) % kPipes; };
+  // Item j of this CTA is blockIdx.x + j * G (phase 0 items first, so a CTA finishes its GEMM1
+  // items before any GEMM2 item). In a split-K phase its K chunks are split over the
+  // pipelines: pipeline p takes the chunks kc with (kc + j) % P == p, into its own accumulator,
+  // and the epilogue sums the partial accumulators (rotating with j balances the pipelines
+  // when P does not divide the chunk count). Otherwise (few chunks per item) item j goes whole
+  // to pipeline j % P, so each item costs one accumulator hand-off instead of P.
+  // jm = j % P; returns the first chunk of pipeline p (k_chunks if it has none).
+  auto chunk_begin = [&](int p, int jm, const PhaseArgs& f) {
+    return f.split_k ? (p - jm + kPipes) % kPipes : (p == jm ? 0 : f.k_chunks);
+  };
+  auto item_phase = [&](int it) -> const PhaseArgs& { return a.ph[it >= n0 ? 1 : 0]; };
 
   if (warp < kMmaWarp0) {
     // ------------------------------------------------------------------ producers
@@ -280,13 +389,21 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
       bool ok = true;
       Ring ws, bs;
       int w_issued = 0, b_issued = 0;
+      // Dependency readiness of this CTA's items j0 .. j0 + 31 (bit j - j0), read 32 counters at
+      // a time so that a satisfied dependency costs no round trip to L2.
+      uint32_t dep_ready = 0;
+      int dep_j0 = -64;
       int jm = 0;
       for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
-        const int kc0 = first_chunk(p, jm);
+        const int it = blockIdx.x + j * G;
+        const PhaseArgs& f = item_phase(it);
+        const int kcn = f.k_chunks, kstep = f.split_k ? kPipes : 1;
+        const int kc0 = chunk_begin(p, jm, f);
         if (kc0 >= kcn) continue;
-        const Item t = decode_item(ctl, offs, blockIdx.x + j * G, n_local, n_box);
-        const size_t tile0 = ((size_t)t.e * a.m_tiles + t.m) * kcn;
-        for (int kc = kc0; kc < kcn; kc += kPipes) {
+        const Item t = decode_item(ctl, offs, it, n0, n_local, n_box, mt0, mt1);
+        const size_t tile0 = ((size_t)t.e * f.m_tiles + t.m) * kcn;
+        bool dep_ok = f.wait_for == nullptr;
+        for (int kc = kc0; kc < kcn; kc += kstep) {
           if (!__all_sync(0xffffffffu, ptx::mbar_wait_sleep(&pc.w_empty[ws.slot], ws.phase ^ 1))) {
             ok = false;
             break;
@@ -294,19 +411,42 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
           uint8_t* wp = w_slot(p, ws.slot);
           if (leader) {
             ptx::mbar_arrive_expect_tx(&pc.w_full[ws.slot], kWStageBytes);
-            ptx::bulk_g2s(wp, a.wq + (tile0 + kc) * kTileCodeBytes, kTileCodeBytes, &pc.w_full[ws.slot]);
-            ptx::bulk_g2s(wp + kTileCodeBytes, a.wsf + (tile0 + kc) * kTileScaleBytes, kTileScaleBytes,
+            ptx::bulk_g2s(wp, f.wq + (tile0 + kc) * kTileCodeBytes, kTileCodeBytes, &pc.w_full[ws.slot]);
+            ptx::bulk_g2s(wp + kTileCodeBytes, f.wsf + (tile0 + kc) * kTileScaleBytes, kTileScaleBytes,
                           &pc.w_full[ws.slot]);
           }
           ++w_issued;
           ws.next(Sw);
+          if (!dep_ok) {
+            // the B rows of this item are written by other CTAs' epilogues (the previous phase):
+            // the weight tile is already on its way, the activation box waits for the counter
+            if (j - dep_j0 >= 32 || !((dep_ready >> (j - dep_j0)) & 1u)) {
+              const int itl = blockIdx.x + (j + lane) * G;
+              bool rdy = false;
+              if (itl < total && itl >= n0) {
+                const Item tl = decode_item(ctl, offs, itl, n0, n_local, n_box, mt0, mt1);
+                rdy = ptx::ld_acquire_gpu(f.wait_for + tl.tile) >= f.wait_target;
+              }
+              dep_ready = __ballot_sync(0xffffffffu, rdy);
+              dep_j0 = j;
+            }
+            dep_ok = (dep_ready >> (j - dep_j0)) & 1u;
+            if (!dep_ok)
+              dep_ok = __all_sync(0xffffffffu, leader ? ptx::wait_counter(f.wait_for + t.tile, f.wait_target) : true);
+            if (!dep_ok) {
+              ok = false;
+              break;
+            }
+            __syncwarp();
+            if (leader) ptx::fence_proxy_async_global();
+          }
           if (!__all_sync(0xffffffffu, ptx::mbar_wait_sleep(&pc.b_empty[bs.slot], bs.phase ^ 1))) {
             ok = false;
             break;
           }
           uint8_t* bp = b_slot(p, bs.slot);
           uint64_t* bb = &pc.b_full[bs.slot];
-          if (a.route_inline) {
+          if (f.b_source == 1) {
             // Activation rows straight from x[token], four rows per gather; only the groups that
             // hold the tile's pairs are loaded (the MMA columns of the rest are never read).
             const int groups = (t.nvalid + 3) >> 2;
@@ -323,9 +463,10 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
               }
             }
           } else if (leader) {
+            const CUtensorMap* tm = f.b_source == 2 ? &tmap_b2 : &tmap_b;
             ptx::mbar_arrive_expect_tx(bb, geo.b_bytes);
-            ptx::tma_load_2d(bp, &tmap_b, kc * kChunkK, t.row0, bb);
-            ptx::tma_load_2d(bp + n_box * 128, &tmap_b, kc * kChunkK + 64, t.row0, bb);
+            ptx::tma_load_2d(bp, tm, kc * kChunkK, t.row0, bb);
+            ptx::tma_load_2d(bp + n_box * 128, tm, kc * kChunkK + 64, t.row0, bb);
           }
           ++b_issued;
           bs.next(Sb);
@@ -370,7 +511,9 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
       uint64_t desc_stage = desc_first;
       int jm = 0;
       for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
-        const int kc0 = first_chunk(p, jm);
+        const PhaseArgs& f = item_phase(blockIdx.x + j * G);
+        const int kcn = f.k_chunks, kstep = f.split_k ? kPipes : 1;
+        const int kc0 = chunk_begin(p, jm, f);
         if (kc0 >= kcn) continue;
         const int acc = accr.slot;
         if (!__all_sync(0xffffffffu, ptx::mbar_wait_sleep(&pc.acc_empty[acc], accr.phase ^ 1))) {
@@ -379,7 +522,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
         }
         ptx::tc_fence_after();
         const uint32_t d_tmem = acc_col0 + acc * n_box;
-        for (int kc = kc0; kc < kcn; kc += kPipes) {
+        for (int kc = kc0; kc < kcn; kc += kstep) {
           const int s = st.slot;
           const int ab = ar.slot;
           const bool ready = ptx::mbar_wait_sleep(&pc.a_full[ab], ar.phase) &&
@@ -421,22 +564,37 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     const uint32_t lane_base = tbase + ((uint32_t)(32 * q) << 16) + geo.n_a * kACols;
     bool ok = true;
     Ring accr[kPipes];
+    // Per-item constants (the item, its global scale, this lane's post-norm weight) are loaded
+    // one item ahead, so their global-memory latency overlaps the previous item.
+    auto item_consts = [&](int it, Item& t, float& gs, float& pnw) {
+      t = decode_item(ctl, offs, it, n0, n_local, n_box, mt0, mt1);
+      const PhaseArgs& f = a.ph[t.ph];
+      gs = __ldg(f.gs + t.e);
+      pnw = f.mode == 2 ? bf16_bits_to_float(__ldg(a.post_norm_w + kTileM * t.m + 32 * q + lane)) : 0.f;
+    };
+    Item t_next;
+    float gs_next = 0.f, pnw_next = 0.f;
+    if (blockIdx.x < total) item_consts(blockIdx.x, t_next, gs_next, pnw_next);
     int jm = 0;
     for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
-      const Item t = decode_item(ctl, offs, blockIdx.x + j * G, n_local, n_box);
-      // partial accumulators of the participating pipelines
+      const Item t = t_next;
+      const float gs_item = gs_next, pnw_item = pnw_next;
+      if (blockIdx.x + (j + 1) * G < total) item_consts(blockIdx.x + (j + 1) * G, t_next, gs_next, pnw_next);
+      const PhaseArgs& f = a.ph[t.ph];
+      const int kcn = f.k_chunks;
+      // accumulators of the participating pipelines
       uint32_t taddr[kPipes];
       int used = 0;
 #pragma unroll
       for (int p = 0; p < kPipes; ++p) {
-        if (first_chunk(p, jm) >= kcn) continue;
-        if (!ptx::mbar_wait_sleep(&ctl.pipe[p].acc_full[accr[p].slot], accr[p].phase)) ok = false;
+        if (chunk_begin(p, jm, f) >= kcn) continue;
+        if (!ptx::mbar_wait(&ctl.pipe[p].acc_full[accr[p].slot], accr[p].phase)) ok = false;
         taddr[used++] = lane_base + p * kPipeCols + accr[p].slot * n_box;
       }
       if (!ok) break;
       ptx::tc_fence_after();
-      const float gsc = a.gs[t.e] * kUnscale;
-      if (a.mode == 1) {
+      const float gsc = gs_item * kUnscale;
+      if (f.mode == 1) {
         const int jj = 64 * t.m + 16 * q + (lane & 15);  // intermediate index of this lane
         for (int cb = 0; cb * 16 < t.nvalid; ++cb) {
           float acc[16];
@@ -460,13 +618,13 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
             if (lane < 16) {
               const float act = mine / (1.0f + __expf(-mine)) * other;
               const __nv_bfloat16 hb = __float2bfloat16_rn(act);
-              a.inter[(size_t)(t.row0 + cb * 16 + col) * a.ld_out + jj] = *reinterpret_cast<const uint16_t*>(&hb);
+              a.inter[(size_t)(t.row0 + cb * 16 + col) * f.ld_out + jj] = *reinterpret_cast<const uint16_t*>(&hb);
             }
           }
         }
       } else {
         const int h = kTileM * t.m + 32 * q + lane;  // output row of this lane
-        const float wn = gsc * (1.0f + bf16_bits_to_float(a.post_norm_w[h]));
+        const float wn = gsc * (1.0f + pnw_item);
         for (int cb = 0; cb * 16 < t.nvalid; ++cb) {
           float acc[16];
           uint32_t v[16];
@@ -485,25 +643,42 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
             const int n = cb * 16 + col;
             if (n < t.nvalid) {  // warp-uniform
               const float y = acc[col] * wn;
-              a.ypart[(size_t)(t.row0 + n) * a.ld_out + h] = y;
+              a.ypart[(size_t)(t.row0 + n) * f.ld_out + h] = y;
               float s2 = y * y;
 #pragma unroll
               for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-              if (lane == 0) a.ssq[(size_t)(t.row0 + n) * (a.ld_out >> 5) + (h >> 5)] = s2;
+              if (lane == 0) a.ssq[(size_t)(t.row0 + n) * (f.ld_out >> 5) + (h >> 5)] = s2;
             }
           }
         }
       }
       ptx::tc_fence_before();
+      if (f.signal && !f.signal_at_end) {
+        // publish this warp's rows of the item: the warp barrier orders every lane's stores
+        // before lane 0's release, which makes them visible GPU-wide before the count
+        __syncwarp();
+        if (lane == 0) ptx::red_release_gpu_add(f.signal + t.tile, 1);
+      }
       __syncwarp();
 #pragma unroll
       for (int p = 0; p < kPipes; ++p) {
-        if (first_chunk(p, jm) >= kcn) continue;
+        if (chunk_begin(p, jm, f) >= kcn) continue;
         if (lane == 0) ptx::mbar_arrive(&ctl.pipe[p].acc_empty[accr[p].slot]);
         accr[p].next(geo.n_acc);
       }
     }
     if (!ok && lane == 0) record_error(a.error_flag, 3);
+    // Counts whose readers only run after every item (the combine) are published here, behind
+    // one fence, instead of one release per item on the epilogue's critical path.
+    if (ok && ((a.ph[0].signal && a.ph[0].signal_at_end) || (a.n_phases > 1 && a.ph[1].signal && a.ph[1].signal_at_end))) {
+      __threadfence();
+      __syncwarp();
+      for (int j = 0; blockIdx.x + j * G < total; ++j) {
+        const Item t = decode_item(ctl, offs, blockIdx.x + j * G, n0, n_local, n_box, mt0, mt1);
+        const PhaseArgs& f = a.ph[t.ph];
+        if (f.signal && f.signal_at_end && lane == 0) atomicAdd(f.signal + t.tile, 1);  // after the fence
+      }
+    }
   } else {
     // ------------------------------------------------------------------ dequantisers
     const int p = (warp - kDeqWarp0) >> 2;
@@ -516,7 +691,9 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     Ring st, ar;
     int jm = 0;
     for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
-      for (int kc = first_chunk(p, jm); kc < kcn; kc += kPipes, st.next(Sw), ar.next(geo.n_a)) {
+      const PhaseArgs& f = item_phase(blockIdx.x + j * G);
+      const int kcn = f.k_chunks, kstep = f.split_k ? kPipes : 1;
+      for (int kc = chunk_begin(p, jm, f); kc < kcn; kc += kstep, st.next(Sw), ar.next(geo.n_a)) {
         const int s = st.slot;
         const int ab = ar.slot;
         if (!ptx::mbar_wait_sleep(&pc.w_full[s], st.phase)) {
@@ -570,6 +747,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
   __syncthreads();
   ptx::tc_fence_after();
   if (warp == kMmaWarp0) ptx::tmem_dealloc(tbase, kTmemCols);
+  if (a.fused) combine_tokens(ctl, a, n_local, n_box);
 }
 
 // Host-side view of one instantiation.
@@ -611,13 +789,13 @@ size_t gemm_smem_bytes(int n_box, int w_stages, int b_stages) {
   return 1024 + (size_t)pick_pipes(n_box) * g.pipe_bytes + sizeof(SharedCtl);
 }
 
-// Ring depths for a token tile: the deepest weight ring that fits 220 KB with one activation
+// Ring depths for a token tile: the deepest weight ring that fits 226 KB with one activation
 // slot more than weight slots (an activation slot lives until its MMAs complete, a weight slot
 // only until it has been read), else equal depths.
 int pick_stages(int n_box, int* b_stages) {
   const int P = pick_pipes(n_box);
   const Geo g = make_geo(pipe_cols(P), n_box, 1, 1);
-  const size_t budget = (220u * 1024u - sizeof(SharedCtl) - 1024) / P;
+  const size_t budget = (226u * 1024u - sizeof(SharedCtl) - 1024) / P;
   for (int sw = kMaxStages; sw >= 2; --sw) {
     for (int extra = 1; extra >= 0; --extra) {
       const int sb = sw + extra;
@@ -631,8 +809,25 @@ int pick_stages(int n_box, int* b_stages) {
   return 2;
 }
 
-int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, const GemmArgs& args,
-                       cudaStream_t stream) {
+template <int P>
+cudaError_t launch_variant(int grid, size_t smem, bool cooperative, const CUtensorMap& tmap_b,
+                           const CUtensorMap& tmap_x, const CUtensorMap& tmap_b2, const GemmArgs& args,
+                           cudaStream_t stream) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(Variant<P>::kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = cooperative ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, expert_gemm_tc<P>, tmap_b, tmap_x, tmap_b2, args);
+}
+
+int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, const CUtensorMap& tmap_b2,
+                       const GemmArgs& args, cudaStream_t stream) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
@@ -650,18 +845,28 @@ int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, con
   }
   if (args.stages < 2 || args.b_stages < 2 || args.stages > kMaxStages || args.b_stages > kMaxStages)
     return MUSE_ERR_UNSUPPORTED_SHAPE;
+  if (args.n_phases < 1 || args.n_phases > 2 || (args.fused && args.n_phases != 2))
+    return MUSE_ERR_INVALID_ARGUMENT;
   const Geo g = make_geo(pipe_cols(pick_pipes(args.n_box)), args.n_box, args.stages, args.b_stages);
   if (g.n_a < 2) return MUSE_ERR_UNSUPPORTED_SHAPE;
   if (args.route_inline &&
       (args.n_pairs > kMaxInlinePairs || args.n_box > kMaxInlineBox || !args.ids || !args.pair_order ||
        !args.pair_row))
     return MUSE_ERR_UNSUPPORTED_SHAPE;
+  // a fused launch combines through the inline routing tables and the GEMM2 tile counters
+  if (args.fused && (!args.route_inline || !args.ph[1].signal || !args.ph[1].wait_for || !args.out ||
+                     !args.topk_weights || args.top_k > kMaxTopK || args.hidden % 128))
+    return MUSE_ERR_INVALID_ARGUMENT;
   const size_t smem = gemm_smem_bytes(args.n_box, args.stages, args.b_stages);
   if (smem > 227u * 1024u) return MUSE_ERR_UNSUPPORTED_SHAPE;
+  const int grid = g_num_sms[dev];
+  // A fused launch waits across CTAs (GEMM2 items on GEMM1 tiles, the combine on GEMM2 tiles):
+  // it is launched cooperatively, so either every CTA is resident at once or the launch fails.
   if (pick_pipes(args.n_box) == 3)
-    expert_gemm_tc<3><<<g_num_sms[dev], Variant<3>::kThreads, smem, stream>>>(tmap_b, tmap_x, args);
+    e = launch_variant<3>(grid, smem, args.fused != 0, tmap_b, tmap_x, tmap_b2, args, stream);
   else
-    expert_gemm_tc<2><<<g_num_sms[dev], Variant<2>::kThreads, smem, stream>>>(tmap_b, tmap_x, args);
+    e = launch_variant<2>(grid, smem, args.fused != 0, tmap_b, tmap_x, tmap_b2, args, stream);
+  if (e != cudaSuccess) return e;
   return last_launch_status();
 }
 

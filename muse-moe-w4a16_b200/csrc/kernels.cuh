@@ -37,34 +37,55 @@ struct ExpertWeights {
   const uint16_t* post_norm_w;  // bf16 bits
 };
 
-// Arguments of one expert-GEMM launch (gemm_tc.cu).
-struct GemmArgs {
-  int32_t* offsets;        // [n_local + 1] expert ranges of the pair rows (written if route_inline)
-  int n_local;
+// One GEMM of a launch (gemm_tc.cu): its weights, its B operand and its epilogue.
+struct PhaseArgs {
   int m_tiles;             // weight rows per expert / 128
   int k_chunks;            // K / 128
-  int n_box;               // token tile = MMA N (16, 32, 64 or 128)
-  int stages;              // weight-tile ring depth (shared memory)
-  int b_stages;            // activation-box ring depth (shared memory)
   const uint8_t* wq;       // prepared codes
   const uint8_t* wsf;      // prepared scales
   const float* gs;         // [n_local] global scales
   int mode;                // 1: SiLU(gate)*up -> inter; 2: post-norm partials -> ypart, ssq
   int ld_out;              // row length of the output (I in mode 1, H in mode 2)
+  int split_k;             // split each item's chunks over the pipelines (else one pipeline per item)
+  int b_source;            // B operand: 0 tmap_b boxes at the tile's rows (expert-grouped rows),
+                           // 1 four-row gathers of x by token (tmap_x), 2 tmap_b2 boxes
+  int* signal;             // per-token-tile counters: each epilogue warp adds 1 per item (or null)
+  int signal_at_end;       // publish the counts after the epilogue's last item, not per item
+  const int* wait_for;     // counters that must reach wait_target before B is loaded (or null)
+  int wait_target;
+};
+
+// Arguments of one expert-GEMM launch. A launch runs one phase (a plain GEMM) or, for small
+// batches, both GEMMs and the combine of the whole layer call (`fused`).
+struct GemmArgs {
+  int32_t* offsets;        // [n_local + 1] expert ranges of the pair rows (written if route_inline)
+  int n_local;
+  int n_box;               // token tile = MMA N (16, 32, 64 or 128)
+  int stages;              // weight-tile ring depth (shared memory)
+  int b_stages;            // activation-box ring depth (shared memory)
+  int n_phases;            // 1 or 2
+  PhaseArgs ph[2];
   uint16_t* inter;
   const uint16_t* post_norm_w;
   float* ypart;
   float* ssq;
   int* error_flag;
   uint32_t mul16, mul64;   // 16 and 64, passed at run time (see dequant8 in gemm_tc.cu)
-  // Small batches, first GEMM only: every CTA groups the pairs itself in its prologue (CTA 0
-  // publishes offsets / pair_order / pair_row for the later kernels) and gathers activation
-  // rows straight from x by token index (tmap_x, one-row box), so no route or gather launch runs.
+  // Small batches: every CTA groups the pairs itself in its prologue (CTA 0 publishes
+  // offsets / pair_order / pair_row) and phase 0 gathers activation rows straight from x.
   int route_inline;
   const int32_t* ids;      // [n_pairs] expert ids (route_inline)
   int n_pairs, local_start, top_k;
   int32_t* pair_order;
   int32_t* pair_row;
+  // fused: after the GEMMs, each CTA combines tokens blockIdx.x, blockIdx.x + G, ... once the
+  // counters ph[1].signal of their tiles reach combine_target.
+  int fused;
+  int combine_target;
+  int tokens, hidden;
+  const float* topk_weights;
+  void* out;
+  int out_f32;
 };
 
 // Largest batch (tokens x top_k) whose routing the first GEMM does in its own prologue, and
@@ -81,8 +102,10 @@ int launch_gather(const uint16_t* x, const int32_t* offsets, const int32_t* pair
 size_t gemm_smem_bytes(int n_box, int w_stages, int b_stages);
 // Weight-ring depth for a token tile; *b_stages receives the activation-ring depth.
 int pick_stages(int n_box, int* b_stages);
-int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, const GemmArgs& args,
-                       cudaStream_t stream);
+// tmap_b / tmap_b2: bf16 row buffers read as n_box-row boxes; tmap_x: x read by four-row gathers.
+// A fused launch is cooperative (all CTAs resident) and needs its counters zeroed beforehand.
+int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, const CUtensorMap& tmap_b2,
+                       const GemmArgs& args, cudaStream_t stream);
 
 // Address of the sticky device status word (current device) and a synchronous read of it.
 int device_status_ptr(int** ptr);

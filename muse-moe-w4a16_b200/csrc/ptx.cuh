@@ -219,6 +219,37 @@ __host__ __device__ constexpr uint32_t idesc_bf16_f32(int m, int n) {
 
 __device__ __forceinline__ uint32_t rotl(uint32_t x, int n) { return __funnelshift_l(x, x, n); }
 
+// ----------------------------------------------------------------------------- cross-CTA flags
+
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// Orders this thread's generic-proxy accesses of global memory with its async-proxy (TMA)
+// accesses: data written with plain stores by one CTA and read by another CTA's TMA.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+// Wait until *p >= target (acquire). Returns false after kWaitCycles.
+__device__ __forceinline__ bool wait_counter(const int* p, int target) {
+  if (ld_acquire_gpu(p) >= target) return true;
+  const long long t0 = clock64();
+  unsigned ns = 32;
+  for (;;) {
+    __nanosleep(ns);
+    if (ns < 256) ns <<= 1;
+    if (ld_acquire_gpu(p) >= target) return true;
+    if (clock64() - t0 > kWaitCycles) return false;
+  }
+}
+
 // One lane of the (fully active) warp is elected; the others get false. The same lane every
 // time for a given warp state, so a role can decide its leader once.
 __device__ __forceinline__ bool elect_one() {

@@ -98,17 +98,18 @@ def test_product_path_does_not_import_oracle():
             assert not re.match(r"\s*(from|import)\s+oracle\b", line), f"{f.name}: {line}"
 
 
-@pytest.mark.parametrize("T,K,E,H,I,launches,inline", [
-    (1, 8, 128, 2048, 768, 3, True), (32, 8, 128, 2048, 768, 3, True),
-    (128, 8, 256, 7168, 2048, 3, True), (129, 8, 256, 7168, 2048, 5, False),
-    (128, 8, 32, 4096, 4096, 5, False), (4, 8, 32, 4096, 4096, 3, True), (0, 8, 32, 4096, 4096, 0, True),
+@pytest.mark.parametrize("T,K,E,H,I,launches,path", [
+    (1, 8, 128, 2048, 768, 1, 2), (16, 8, 128, 2048, 768, 1, 2), (32, 8, 128, 2048, 768, 3, 1),
+    (128, 8, 256, 7168, 2048, 3, 1), (129, 8, 256, 7168, 2048, 5, 0),
+    (128, 8, 32, 4096, 4096, 5, 0), (4, 8, 32, 4096, 4096, 1, 2), (0, 8, 32, 4096, 4096, 0, 2),
 ])
-def test_launch_plan(pkg, T, K, E, H, I, launches, inline):
-    """Batches of <= 1024 pairs whose token tile is <= 32 run three kernels (routing and the
-    activation gather inside GEMM1); everything else runs route, gather, GEMM1, GEMM2, combine."""
+def test_launch_plan(pkg, T, K, E, H, I, launches, path):
+    """<= 128 pairs with a token tile <= 32: the whole layer in one cooperative launch;
+    <= 1024 pairs: GEMM1 routes and gathers x itself, then GEMM2 and the combine; larger
+    batches: route, gather, GEMM1, GEMM2, combine."""
     from muse_moe_w4a16_b200 import _lib
     plan = _lib.launch_plan(T, K, E, H, I)
-    assert plan["launches"] == launches and plan["route_inline"] == inline
+    assert plan["launches"] == launches and plan["path"] == path
     assert plan["n_box"] in (16, 32, 64, 128) and plan["stages"] >= 2
 
 
