@@ -254,7 +254,9 @@ __device__ __forceinline__ void combine_tokens(SharedCtl& ctl, const GemmArgs& a
   }
 }
 
-template <int P>
+// kFused: the single-launch variant (two phases with cross-CTA tile counters, then the
+// combine). The plain variant leaves that code out of its loops.
+template <int P, bool kFused>
 __global__ void __launch_bounds__(Roles<P>::kThreads, 1)
 expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_x,
                const __grid_constant__ CUtensorMap tmap_b2, const GemmArgs a) {
@@ -302,7 +304,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
   }
   if (warp < kPipes && lane == 0) {
     ptx::prefetch_tensormap(a.route_inline ? &tmap_x : &tmap_b);
-    if (a.n_phases > 1) ptx::prefetch_tensormap(&tmap_b2);
+    if (kFused) ptx::prefetch_tensormap(&tmap_b2);
   }
   // Expert ranges: from the route kernel, or (small batches) computed here by every CTA, with
   // the stage buffers as scratch -- nothing is copied into them before the prologue ends.
@@ -362,7 +364,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
 
   const uint32_t tbase = ctl.tmem_base;
   const int tiles = ctl.tile_prefix[n_local];
-  const int mt0 = a.ph[0].m_tiles, mt1 = a.n_phases > 1 ? a.ph[1].m_tiles : 0;
+  const int mt0 = a.ph[0].m_tiles, mt1 = kFused ? a.ph[1].m_tiles : 0;
   const int n0 = tiles * mt0;                       // items of phase 0
   const int total = n0 + tiles * mt1;               // all items of this launch
   const int G = gridDim.x;
@@ -376,7 +378,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
   auto chunk_begin = [&](int p, int jm, const PhaseArgs& f) {
     return f.split_k ? (p - jm + kPipes) % kPipes : (p == jm ? 0 : f.k_chunks);
   };
-  auto item_phase = [&](int it) -> const PhaseArgs& { return a.ph[it >= n0 ? 1 : 0]; };
+  auto item_phase = [&](int it) -> const PhaseArgs& { return a.ph[kFused && it >= n0 ? 1 : 0]; };
 
   if (warp < kMmaWarp0) {
     // ------------------------------------------------------------------ producers
@@ -402,7 +404,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
         if (kc0 >= kcn) continue;
         const Item t = decode_item(ctl, offs, it, n0, n_local, n_box, mt0, mt1);
         const size_t tile0 = ((size_t)t.e * f.m_tiles + t.m) * kcn;
-        bool dep_ok = f.wait_for == nullptr;
+        bool dep_ok = !kFused || f.wait_for == nullptr;
         for (int kc = kc0; kc < kcn; kc += kstep) {
           if (!__all_sync(0xffffffffu, ptx::mbar_wait_sleep(&pc.w_empty[ws.slot], ws.phase ^ 1))) {
             ok = false;
@@ -588,7 +590,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
 #pragma unroll
       for (int p = 0; p < kPipes; ++p) {
         if (chunk_begin(p, jm, f) >= kcn) continue;
-        if (!ptx::mbar_wait(&ctl.pipe[p].acc_full[accr[p].slot], accr[p].phase)) ok = false;
+        if (!ptx::mbar_wait_sleep(&ctl.pipe[p].acc_full[accr[p].slot], accr[p].phase)) ok = false;
         taddr[used++] = lane_base + p * kPipeCols + accr[p].slot * n_box;
       }
       if (!ok) break;
@@ -653,7 +655,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
         }
       }
       ptx::tc_fence_before();
-      if (f.signal && !f.signal_at_end) {
+      if (kFused && f.signal) {
         // publish this warp's rows of the item: the warp barrier orders every lane's stores
         // before lane 0's release, which makes them visible GPU-wide before the count
         __syncwarp();
@@ -668,17 +670,6 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
       }
     }
     if (!ok && lane == 0) record_error(a.error_flag, 3);
-    // Counts whose readers only run after every item (the combine) are published here, behind
-    // one fence, instead of one release per item on the epilogue's critical path.
-    if (ok && ((a.ph[0].signal && a.ph[0].signal_at_end) || (a.n_phases > 1 && a.ph[1].signal && a.ph[1].signal_at_end))) {
-      __threadfence();
-      __syncwarp();
-      for (int j = 0; blockIdx.x + j * G < total; ++j) {
-        const Item t = decode_item(ctl, offs, blockIdx.x + j * G, n0, n_local, n_box, mt0, mt1);
-        const PhaseArgs& f = a.ph[t.ph];
-        if (f.signal && f.signal_at_end && lane == 0) atomicAdd(f.signal + t.tile, 1);  // after the fence
-      }
-    }
   } else {
     // ------------------------------------------------------------------ dequantisers
     const int p = (warp - kDeqWarp0) >> 2;
@@ -747,7 +738,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
   __syncthreads();
   ptx::tc_fence_after();
   if (warp == kMmaWarp0) ptx::tmem_dealloc(tbase, kTmemCols);
-  if (a.fused) combine_tokens(ctl, a, n_local, n_box);
+  if (kFused) combine_tokens(ctl, a, n_local, n_box);
 }
 
 // Host-side view of one instantiation.
@@ -809,7 +800,7 @@ int pick_stages(int n_box, int* b_stages) {
   return 2;
 }
 
-template <int P>
+template <int P, bool kFused>
 cudaError_t launch_variant(int grid, size_t smem, bool cooperative, const CUtensorMap& tmap_b,
                            const CUtensorMap& tmap_x, const CUtensorMap& tmap_b2, const GemmArgs& args,
                            cudaStream_t stream) {
@@ -823,7 +814,7 @@ cudaError_t launch_variant(int grid, size_t smem, bool cooperative, const CUtens
   attr[0].val.cooperative = cooperative ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, expert_gemm_tc<P>, tmap_b, tmap_x, tmap_b2, args);
+  return cudaLaunchKernelEx(&cfg, expert_gemm_tc<P, kFused>, tmap_b, tmap_x, tmap_b2, args);
 }
 
 int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, const CUtensorMap& tmap_b2,
@@ -837,9 +828,10 @@ int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, con
     if (e != cudaSuccess) return e;
   }
   if (!g_attr_set[dev]) {
-    e = cudaFuncSetAttribute(expert_gemm_tc<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e == cudaSuccess)
-      e = cudaFuncSetAttribute(expert_gemm_tc<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    const void* fns[4] = {(const void*)expert_gemm_tc<2, false>, (const void*)expert_gemm_tc<3, false>,
+                          (const void*)expert_gemm_tc<2, true>, (const void*)expert_gemm_tc<3, true>};
+    for (int i = 0; i < 4 && e == cudaSuccess; ++i)
+      e = cudaFuncSetAttribute(fns[i], cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
     g_attr_set[dev] = true;
   }
@@ -862,10 +854,13 @@ int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, con
   const int grid = g_num_sms[dev];
   // A fused launch waits across CTAs (GEMM2 items on GEMM1 tiles, the combine on GEMM2 tiles):
   // it is launched cooperatively, so either every CTA is resident at once or the launch fails.
-  if (pick_pipes(args.n_box) == 3)
-    e = launch_variant<3>(grid, smem, args.fused != 0, tmap_b, tmap_x, tmap_b2, args, stream);
+  const bool three = pick_pipes(args.n_box) == 3;
+  if (args.fused)
+    e = three ? launch_variant<3, true>(grid, smem, true, tmap_b, tmap_x, tmap_b2, args, stream)
+              : launch_variant<2, true>(grid, smem, true, tmap_b, tmap_x, tmap_b2, args, stream);
   else
-    e = launch_variant<2>(grid, smem, args.fused != 0, tmap_b, tmap_x, tmap_b2, args, stream);
+    e = three ? launch_variant<3, false>(grid, smem, false, tmap_b, tmap_x, tmap_b2, args, stream)
+              : launch_variant<2, false>(grid, smem, false, tmap_b, tmap_x, tmap_b2, args, stream);
   if (e != cudaSuccess) return e;
   return last_launch_status();
 }

@@ -50,7 +50,6 @@ struct PhaseArgs {
   int b_source;            // B operand: 0 tmap_b boxes at the tile's rows (expert-grouped rows),
                            // 1 four-row gathers of x by token (tmap_x), 2 tmap_b2 boxes
   int* signal;             // per-token-tile counters: each epilogue warp adds 1 per item (or null)
-  int signal_at_end;       // publish the counts after the epilogue's last item, not per item
   const int* wait_for;     // counters that must reach wait_target before B is loaded (or null)
   int wait_target;
 };
