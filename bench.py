@@ -22,6 +22,7 @@ path restated in numpy, all host cores) on the same workload; rank 0 only.
 from __future__ import annotations
 
 import argparse
+import faulthandler
 import json
 import math
 import os
@@ -452,6 +453,7 @@ def run_muse(args, world, rank, local):
 
 
 def main(argv=None):
+    faulthandler.enable()   # a crash prints the Python stack of every thread
     args = parse_args(argv)
     world, rank, local = dist_setup(args.gpus)
     try:

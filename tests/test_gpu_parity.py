@@ -174,12 +174,14 @@ def test_layer_cuda_graph_replay(pkg, synth, cfg2_weights):
         assert ok, msg
 
 
-def test_layer_cfg4_large_expert_sampled_rows(pkg, synth):
-    """E=256, H=7168, I=2048 at T=32: every token is computed on the GPU, 3 rows are checked
-    against the oracle (the oracle dequantises only their experts)."""
-    shape = synth.CONFIGS["cfg4"]
-    data = synth.baseline_input(shape, 32, seed=4032)
-    rows = [0, 13, 31]
+@pytest.mark.parametrize("workload,T,rows", [("cfg4", 32, [0, 13, 31]), ("cfg4", 256, [0, 100, 255]),
+                                             ("cfg5", 4096, [0, 1777, 4095])])
+def test_layer_cfg4_large_expert_sampled_rows(pkg, synth, workload, T, rows):
+    """E=256, H=7168, I=2048 at decode (T=32, 256: one and three launches) and prefill (T=4096,
+    Zipf router, 128-token tiles, five launches): every token is computed on the GPU, 3 rows are
+    checked against the oracle (the oracle dequantises only their experts)."""
+    shape = synth.CONFIGS[workload]
+    data = synth.baseline_input(shape, T, seed=4000 + T)
     need = sorted(set(data["topk_ids"][rows].reshape(-1).tolist()))
     w = synth.baseline_weights(shape, seed=5252, device="cuda")
     w_np = to_numpy_weights({k: (v[need] if v.dim() > 1 or k.endswith("_gs") else v) for k, v in w.items()})
