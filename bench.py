@@ -302,20 +302,22 @@ def run_muse(args, world, rank, local):
             g = _Eager(lambda d=d: layer_call(d))
         graphs[t] = g
 
-    # End-to-end graphs: pinned host inputs -> device, kernel_fn, result -> pinned host.
-    e2e_graphs, h2d, d2h = {}, 0, 0
-    host_in, host_out = {}, {}
-    for t in tokens:
+    # End-to-end: pinned host inputs -> device, layer call, result -> pinned host. One graph
+    # per token count, built, timed and released in turn (see e2e_time below).
+    h2d = sum(inputs[t][k].numel() * inputs[t][k].element_size()
+              for t in tokens for k in ("hidden_states", "topk_ids", "topk_weights"))
+    d2h = sum(t * shape.hidden * 2 for t in tokens)
+
+    def e2e_graph(t):
         hi = {k: (v.pin_memory() if isinstance(v, torch.Tensor) else v) for k, v in inputs[t].items()}
-        host_in[t] = hi
-        host_out[t] = torch.empty((t, shape.hidden), dtype=torch.bfloat16).pin_memory()
+        ho = torch.empty((t, shape.hidden), dtype=torch.bfloat16).pin_memory()
         d = {k: (torch.empty_like(v, device=dev) if isinstance(v, torch.Tensor) else v) for k, v in hi.items()}
         for k in ("hidden_states", "topk_ids", "topk_weights"):
             d[k].copy_(hi[k], non_blocking=True)
         layer_call(d)
         torch.cuda.synchronize()
 
-        def e2e_step(d=d, hi=hi, ho=host_out[t]):
+        def e2e_step():
             for k in ("hidden_states", "topk_ids", "topk_weights"):
                 d[k].copy_(hi[k], non_blocking=True)
             ho.copy_(layer_call(d), non_blocking=True)
@@ -326,9 +328,7 @@ def run_muse(args, world, rank, local):
                 e2e_step()
         else:
             g = _Eager(e2e_step)
-        e2e_graphs[t] = g
-        h2d += sum(hi[k].numel() * hi[k].element_size() for k in ("hidden_states", "topk_ids", "topk_weights"))
-        d2h += host_out[t].numel() * 2
+        return g, (hi, ho, d)
 
     def timed(graph_map, steps):
         ev = {t: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
@@ -343,7 +343,6 @@ def run_muse(args, world, rank, local):
 
     # warm-up (untimed)
     timed(graphs, args.warmup)
-    timed(e2e_graphs, max(1, args.warmup))
     torch.cuda.synchronize()
 
     with ClockSampler(local) as clocks:
@@ -352,8 +351,24 @@ def run_muse(args, world, rank, local):
         ev = timed(graphs, args.steps)
         torch.cuda.synchronize()
         barrier(world)
-    ev_e2e = timed(e2e_graphs, args.steps)
-    torch.cuda.synchronize()
+    # One end-to-end graph alive at a time: a process holding the layer graphs plus every
+    # token count's end-to-end graph at once (cfg3: T = 128, 256, 512) crashed inside the graph
+    # launch on this pool, while any subset ran clean.
+    per_t_e2e = []
+    for t in tokens:
+        g, keep = e2e_graph(t)
+        evs = []
+        for i in range(max(1, args.warmup) + args.steps):
+            flush.zero_()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            g.replay()
+            e1.record(stream)
+            if i >= max(1, args.warmup):
+                evs.append((e0, e1))
+        torch.cuda.synchronize()
+        per_t_e2e.append(statistics.mean(a.elapsed_time(b) * 1e3 for a, b in evs))
+        del g, keep
 
     # Per-kernel times: the same calls, eager, with events recorded between the kernels (the
     # 512 MiB flush in front of each call keeps the GPU behind the host, so no event waits on
@@ -373,7 +388,6 @@ def run_muse(args, world, rank, local):
                     for t in tokens}
 
     per_t = [statistics.mean(a.elapsed_time(b) * 1e3 for a, b in ev[t]) for t in tokens]
-    per_t_e2e = [statistics.mean(a.elapsed_time(b) * 1e3 for a, b in ev_e2e[t]) for t in tokens]
     per_t = max_over_ranks(world, per_t)
     per_t_e2e = max_over_ranks(world, per_t_e2e)
     flat = max_over_ranks(world, [v for t in tokens for v in stage_us[t]])
@@ -447,7 +461,7 @@ def run_muse(args, world, rank, local):
         line["cpu_baseline"] = cpu_baseline(shape, tokens, w, inputs)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del graphs, e2e_graphs   # graphs holding NCCL calls go before the process group
+    del graphs   # graphs holding NCCL calls go before the process group
     torch.cuda.synchronize()
     return 0
 

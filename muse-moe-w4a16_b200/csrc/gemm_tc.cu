@@ -304,7 +304,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
   }
   if (warp < kPipes && lane == 0) {
     ptx::prefetch_tensormap(a.route_inline ? &tmap_x : &tmap_b);
-    if (kFused) ptx::prefetch_tensormap(&tmap_b2);
+    if (kFused && a.n_phases > 1) ptx::prefetch_tensormap(&tmap_b2);
   }
   // Expert ranges: from the route kernel, or (small batches) computed here by every CTA, with
   // the stage buffers as scratch -- nothing is copied into them before the prologue ends.
@@ -364,7 +364,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
 
   const uint32_t tbase = ctl.tmem_base;
   const int tiles = ctl.tile_prefix[n_local];
-  const int mt0 = a.ph[0].m_tiles, mt1 = kFused ? a.ph[1].m_tiles : 0;
+  const int mt0 = a.ph[0].m_tiles, mt1 = kFused && a.n_phases > 1 ? a.ph[1].m_tiles : 0;
   const int n0 = tiles * mt0;                       // items of phase 0
   const int total = n0 + tiles * mt1;               // all items of this launch
   const int G = gridDim.x;
@@ -738,7 +738,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
   __syncthreads();
   ptx::tc_fence_after();
   if (warp == kMmaWarp0) ptx::tmem_dealloc(tbase, kTmemCols);
-  if (kFused) combine_tokens(ctl, a, n_local, n_box);
+  if (kFused && a.fused) combine_tokens(ctl, a, n_local, n_box);
 }
 
 // Host-side view of one instantiation.
