@@ -37,14 +37,21 @@ namespace muse {
 namespace {
 
 constexpr int kMaxPipes = 3;
+// The 16-token (decode) tile's layout: pipelines x dequant warps per pipeline. Measured on
+// B200 (cfg2 / cfg4 decode sweeps): 3 x 4 beats 2 x 8 (two warps per lane quarter) by 2-10 %.
+constexpr int kDecodePipes = 3;
+constexpr int kDecodeDW = 4;
 constexpr int kACols = kChunkK / 2;   // TMEM columns per A buffer (bf16 pairs)
 constexpr int kTmemCols = 512;
 
-template <int P> struct Roles {
+// P pipelines, DW dequant warps per pipeline (4: one per TMEM lane quarter, each converting a
+// whole 128-element row slice of a chunk; 8: two per quarter, each converting one half).
+template <int P, int DW> struct Roles {
+  static_assert(DW == 4 || DW == 8, "dequant warps per pipeline");
   static constexpr int kMmaWarp0 = P;
   static constexpr int kEpiWarp0 = 2 * P;
-  static constexpr int kDeqWarp0 = 2 * P + 4;
-  static constexpr int kWarps = 2 * P + 4 + 4 * P;
+  static constexpr int kDeqWarp0 = 2 * P + 4;  // a multiple of 4 for P = 2: warp % 4 = quarter
+  static constexpr int kWarps = 2 * P + 4 + DW * P;
   static constexpr int kThreads = 32 * kWarps;
   static constexpr int kPipeCols = (kTmemCols / P) / 32 * 32;
 };
@@ -256,11 +263,11 @@ __device__ __forceinline__ void combine_tokens(SharedCtl& ctl, const GemmArgs& a
 
 // kFused: the single-launch variant (two phases with cross-CTA tile counters, then the
 // combine). The plain variant leaves that code out of its loops.
-template <int P, bool kFused>
-__global__ void __launch_bounds__(Roles<P>::kThreads, 1)
+template <int P, int DW, bool kFused>
+__global__ void __launch_bounds__(Roles<P, DW>::kThreads, 1)
 expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_x,
                const __grid_constant__ CUtensorMap tmap_b2, const GemmArgs a) {
-  using R = Roles<P>;
+  using R = Roles<P, DW>;
   constexpr int kPipes = P;
   constexpr int kMmaWarp0 = R::kMmaWarp0, kEpiWarp0 = R::kEpiWarp0, kDeqWarp0 = R::kDeqWarp0;
   constexpr int kPipeCols = R::kPipeCols;
@@ -284,14 +291,14 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
       PipeCtl& pc = ctl.pipe[p];
       for (int s = 0; s < Sw; ++s) {
         ptx::mbar_init(&pc.w_full[s], 1);
-        ptx::mbar_init(&pc.w_empty[s], 4);  // the 4 dequant warps
+        ptx::mbar_init(&pc.w_empty[s], DW);  // the dequant warps
       }
       for (int s = 0; s < Sb; ++s) {
         ptx::mbar_init(&pc.b_full[s], 1);
         ptx::mbar_init(&pc.b_empty[s], 1);  // MMA commit
       }
       for (int b = 0; b < geo.n_a; ++b) {
-        ptx::mbar_init(&pc.a_full[b], 4);
+        ptx::mbar_init(&pc.a_full[b], DW);
         ptx::mbar_init(&pc.a_empty[b], 1);
       }
       for (int b = 0; b < 2; ++b) {
@@ -672,9 +679,10 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     if (!ok && lane == 0) record_error(a.error_flag, 3);
   } else {
     // ------------------------------------------------------------------ dequantisers
-    const int p = (warp - kDeqWarp0) >> 2;
+    const int p = (warp - kDeqWarp0) / DW;
     PipeCtl& pc = ctl.pipe[p];
     const int q = warp & 3;                  // TMEM lane quarter
+    const int hsel = DW == 8 ? ((warp - kDeqWarp0) % DW) >> 2 : 0;  // DW = 8: this warp's half
     const int row = 32 * q + lane;           // weight row of this thread
     const uint32_t lane_col0 = tbase + ((uint32_t)(32 * q) << 16) + p * kPipeCols;
     const uint32_t m16 = a.mul16, m64 = a.mul64;
@@ -695,9 +703,11 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
         // the producer before doing any arithmetic
         const uint8_t* wp = w_slot(p, s);
         const uint8_t* arow = wp + row * kRowCodeBytes;
-        uint4 cw[4];
+        constexpr int kHalves = DW == 8 ? 1 : 2;  // halves of the chunk this warp converts
+        uint4 cw[2 * kHalves];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) cw[c] = *reinterpret_cast<const uint4*>(arow + 16 * code_slot(row, c));
+        for (int c = 0; c < 2 * kHalves; ++c)
+          cw[c] = *reinterpret_cast<const uint4*>(arow + 16 * code_slot(row, 2 * hsel + c));
         const uint2 sfw = *reinterpret_cast<const uint2*>(wp + kTileCodeBytes + row * kRowScaleBytes);
         __syncwarp();
         if (lane == 0) ptx::mbar_arrive(&pc.w_empty[s]);
@@ -706,9 +716,10 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
           break;
         }
 #pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const uint4 c0 = cw[2 * half];
-          const uint4 c1 = cw[2 * half + 1];
+        for (int hh = 0; hh < kHalves; ++hh) {
+          const int half = hsel + hh;
+          const uint4 c0 = cw[2 * hh];
+          const uint4 c1 = cw[2 * hh + 1];
           const uint32_t sw = half ? sfw.y : sfw.x;  // the 4 scale bytes of these 64 elements
           const uint32_t sc[4] = {ctl.scale_lut[__byte_perm(sw, 0, 0x4440)],
                                   ctl.scale_lut[__byte_perm(sw, 0, 0x4441)],
@@ -742,9 +753,9 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
 }
 
 // Host-side view of one instantiation.
-template <int P> struct Variant {
-  static constexpr int kThreads = Roles<P>::kThreads;
-  static constexpr int kPipeCols = Roles<P>::kPipeCols;
+template <int P, int DW> struct Variant {
+  static constexpr int kThreads = Roles<P, DW>::kThreads;
+  static constexpr int kPipeCols = Roles<P, DW>::kPipeCols;
 };
 
 int g_num_sms[64] = {0};
@@ -771,9 +782,12 @@ int read_device_status(int* status, int reset) {
 }
 
 // Pipelines per CTA for a token tile: three issuers fit the tensor memory only with N = 16.
-int pick_pipes(int n_box) { return n_box <= 16 ? 3 : 2; }
+int pick_pipes(int n_box) { return n_box <= 16 ? kDecodePipes : 2; }
+// Dequant warps per pipeline for a token tile.
+int pick_dw(int n_box) { return n_box <= 16 ? kDecodeDW : 4; }
 
-int pipe_cols(int pipes) { return pipes == 3 ? Variant<3>::kPipeCols : Variant<2>::kPipeCols; }
+int pipe_cols(int pipes) { return pipes == 3 ? Variant<3, 4>::kPipeCols : Variant<2, 4>::kPipeCols; }
+static_assert(kDecodePipes == 2 || kDecodePipes == 3, "decode pipelines");
 
 size_t gemm_smem_bytes(int n_box, int w_stages, int b_stages) {
   const Geo g = make_geo(pipe_cols(pick_pipes(n_box)), n_box, w_stages, b_stages);
@@ -800,13 +814,13 @@ int pick_stages(int n_box, int* b_stages) {
   return 2;
 }
 
-template <int P, bool kFused>
+template <int P, int DW, bool kFused>
 cudaError_t launch_variant(int grid, size_t smem, bool cooperative, const CUtensorMap& tmap_b,
                            const CUtensorMap& tmap_x, const CUtensorMap& tmap_b2, const GemmArgs& args,
                            cudaStream_t stream) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(grid);
-  cfg.blockDim = dim3(Variant<P>::kThreads);
+  cfg.blockDim = dim3(Variant<P, DW>::kThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -814,7 +828,7 @@ cudaError_t launch_variant(int grid, size_t smem, bool cooperative, const CUtens
   attr[0].val.cooperative = cooperative ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, expert_gemm_tc<P, kFused>, tmap_b, tmap_x, tmap_b2, args);
+  return cudaLaunchKernelEx(&cfg, expert_gemm_tc<P, DW, kFused>, tmap_b, tmap_x, tmap_b2, args);
 }
 
 int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, const CUtensorMap& tmap_b2,
@@ -828,8 +842,9 @@ int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, con
     if (e != cudaSuccess) return e;
   }
   if (!g_attr_set[dev]) {
-    const void* fns[4] = {(const void*)expert_gemm_tc<2, false>, (const void*)expert_gemm_tc<3, false>,
-                          (const void*)expert_gemm_tc<2, true>, (const void*)expert_gemm_tc<3, true>};
+    const void* fns[4] = {(const void*)expert_gemm_tc<2, 4, false>, (const void*)expert_gemm_tc<2, 4, true>,
+                          (const void*)expert_gemm_tc<kDecodePipes, kDecodeDW, false>,
+                          (const void*)expert_gemm_tc<kDecodePipes, kDecodeDW, true>};
     for (int i = 0; i < 4 && e == cudaSuccess; ++i)
       e = cudaFuncSetAttribute(fns[i], cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
@@ -854,13 +869,13 @@ int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, con
   const int grid = g_num_sms[dev];
   // A fused launch waits across CTAs (GEMM2 items on GEMM1 tiles, the combine on GEMM2 tiles):
   // it is launched cooperatively, so either every CTA is resident at once or the launch fails.
-  const bool three = pick_pipes(args.n_box) == 3;
+  const bool decode = args.n_box <= 16;  // the decode variant: kDecodePipes x kDecodeDW
   if (args.fused)
-    e = three ? launch_variant<3, true>(grid, smem, true, tmap_b, tmap_x, tmap_b2, args, stream)
-              : launch_variant<2, true>(grid, smem, true, tmap_b, tmap_x, tmap_b2, args, stream);
+    e = decode ? launch_variant<kDecodePipes, kDecodeDW, true>(grid, smem, true, tmap_b, tmap_x, tmap_b2, args, stream)
+               : launch_variant<2, 4, true>(grid, smem, true, tmap_b, tmap_x, tmap_b2, args, stream);
   else
-    e = three ? launch_variant<3, false>(grid, smem, false, tmap_b, tmap_x, tmap_b2, args, stream)
-              : launch_variant<2, false>(grid, smem, false, tmap_b, tmap_x, tmap_b2, args, stream);
+    e = decode ? launch_variant<kDecodePipes, kDecodeDW, false>(grid, smem, false, tmap_b, tmap_x, tmap_b2, args, stream)
+               : launch_variant<2, 4, false>(grid, smem, false, tmap_b, tmap_x, tmap_b2, args, stream);
   if (e != cudaSuccess) return e;
   return last_launch_status();
 }
