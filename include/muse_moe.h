@@ -143,6 +143,20 @@ int muse_moe_forward_partial(const void* x, const int32_t* topk_ids, const float
 int muse_moe_cast_bf16(const float* in, void* out, size_t n, muse_stream_t stream);
 
 /*
+ * The decode-layout exchange of an expert-parallel layer over NVLink peer memory:
+ * out (bf16 [n], this rank) = sum over ranks r = 0 .. ranks-1, in that order, of shares[r]
+ * (fp32 [n] each, the ranks' muse_moe_forward_partial outputs). shares[r] and flags[r] are
+ * device addresses valid on this GPU (peer mappings of every rank's symmetric buffers, this
+ * rank's own included); flags[r] is rank r's array of 8 uint32 slots, zero before the first
+ * call. Every rank calls it with the same gen = 1, 2, 3, ... and alternates its share buffer
+ * by gen parity. Waits for the peers are bounded (~1 s); on expiry the output is left
+ * untouched and muse_moe_device_status reports 6. Replaces the all-reduce that sums the ep8
+ * ranks' partial outputs (reference.py:18-22, TASK.md:29 run one rank per GPU).
+ */
+int muse_moe_peer_allreduce_bf16(const uint64_t* shares, const uint64_t* flags, int ranks, int rank,
+                                 uint32_t gen, size_t n, void* out, muse_stream_t stream);
+
+/*
  * muse_moe_forward, with five caller-created CUDA events (cudaEvent_t, passed as void*)
  * recorded on `stream` around the kernels: [0] start, [1] before GEMM1, [2] after GEMM1,
  * [3] after GEMM2, [4] after the combine. For per-kernel timing; same results as

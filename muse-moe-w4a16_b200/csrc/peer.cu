@@ -1,0 +1,117 @@
+// Expert-parallel exchange over NVLink peer memory: the sum of every rank's fp32 share of the
+// layer output, cast to bf16, on every rank (the all-reduce of the decode layout, done by
+// this kernel instead of a collective library).
+//
+// Each rank's share lives in its own symmetric buffer; the buffers of all ranks are mapped
+// into every rank's address space (peer pointers). A call with generation `gen` (1, 2, ...,
+// the same on every rank) proceeds in three steps:
+//   1. block 0 publishes "my share of call gen is complete" by writing gen into slot `rank`
+//      of every rank's flag array (system-scope release after a system fence, so the share's
+//      bytes -- written by the previous kernel on this stream -- are visible first);
+//   2. every block waits (acquire, bounded) until all R slots of its own flag array hold gen;
+//   3. out[i] = bf16(sum over r = 0 .. R-1 of share_r[i]), the same order on every rank, so
+//      all ranks produce identical bits.
+// Callers alternate between two share buffers by gen parity: a rank rewrites a buffer only two
+// calls later, after every peer has signalled the call in between (which it does only after
+// finishing its reads of this rank's older share).
+#include "common.cuh"
+#include "kernels.cuh"
+#include "ptx.cuh"
+
+namespace muse {
+namespace {
+
+constexpr int kMaxPeers = 8;
+
+struct PeerArgs {
+  const float* share[kMaxPeers];  // share of rank r (peer pointers, this rank's own included)
+  uint32_t* flags[kMaxPeers];     // flag array of rank r (kMaxPeers slots each)
+  int ranks, rank;
+  uint32_t gen;
+  size_t n4;                      // elements / 4
+  uint16_t* out;                  // bf16 [n], this rank's memory
+  int* error_flag;
+};
+
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__global__ void __launch_bounds__(256) peer_allreduce_kernel(const PeerArgs a) {
+  __shared__ int s_ok;
+  if (blockIdx.x == 0 && threadIdx.x < a.ranks) {
+    __threadfence_system();
+    st_release_sys(a.flags[threadIdx.x] + a.rank, a.gen);
+  }
+  if (threadIdx.x == 0) {
+    const uint32_t* mine = a.flags[a.rank];
+    bool ok = true;
+    const long long t0 = clock64();
+    for (int r = 0; r < a.ranks && ok; ++r) {
+      unsigned ns = 32;
+      while (ld_acquire_sys(mine + r) < a.gen) {
+        if (clock64() - t0 > ptx::kWaitCycles) {
+          ok = false;
+          break;
+        }
+        __nanosleep(ns);
+        if (ns < 256) ns <<= 1;
+      }
+    }
+    if (!ok) atomicExch(a.error_flag, 6);
+    s_ok = ok;
+  }
+  __syncthreads();
+  if (!s_ok) return;  // a peer never signalled: leave the output alone, the status says why
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < a.n4; i += (size_t)gridDim.x * blockDim.x) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r = 0; r < a.ranks; ++r) {
+      const float4 v = __ldcv(reinterpret_cast<const float4*>(a.share[r]) + i);
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
+    __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
+    uint2 packed;
+    packed.x = *reinterpret_cast<uint32_t*>(&lo);
+    packed.y = *reinterpret_cast<uint32_t*>(&hi);
+    reinterpret_cast<uint2*>(a.out)[i] = packed;
+  }
+}
+
+}  // namespace
+}  // namespace muse
+
+extern "C" int muse_moe_peer_allreduce_bf16(const uint64_t* shares, const uint64_t* flags, int ranks,
+                                            int rank, uint32_t gen, size_t n, void* out,
+                                            muse_stream_t stream) {
+  using namespace muse;
+  if (!shares || !flags || !out || ranks < 1 || ranks > kMaxPeers || rank < 0 || rank >= ranks ||
+      gen == 0 || n % 8)
+    return MUSE_ERR_INVALID_ARGUMENT;
+  PeerArgs a{};
+  for (int r = 0; r < ranks; ++r) {
+    if (!shares[r] || !flags[r] || shares[r] % 16 || flags[r] % 4) return MUSE_ERR_INVALID_ARGUMENT;
+    a.share[r] = reinterpret_cast<const float*>(shares[r]);
+    a.flags[r] = reinterpret_cast<uint32_t*>(flags[r]);
+  }
+  if (reinterpret_cast<uintptr_t>(out) % 16) return MUSE_ERR_INVALID_ARGUMENT;
+  a.ranks = ranks;
+  a.rank = rank;
+  a.gen = gen;
+  a.n4 = n / 4;
+  a.out = static_cast<uint16_t*>(out);
+  int rc = device_status_ptr(&a.error_flag);
+  if (rc) return rc;
+  const size_t blocks = (a.n4 + 255) / 256;
+  peer_allreduce_kernel<<<blocks < 296 ? (unsigned)blocks : 296u, 256, 0, (cudaStream_t)stream>>>(a);
+  return last_launch_status();
+}

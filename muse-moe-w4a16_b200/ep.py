@@ -1,26 +1,31 @@
 """Expert parallelism across the GPUs of one node: one process per GPU, experts split into
-contiguous blocks, NCCL for the exchange.
+contiguous blocks; the decode exchange runs over NVLink peer memory, the prefill one on NCCL.
 
 The reference's problem is always expert-parallel: GPU r holds experts
 [32r, 32r + 32) and computes only their (token, slot) pairs (reference.py:18-22, TASK.md:29).
 Here a rank computes the fp32 sum of its local slots for the tokens it sees
-(`kernel_fn_partial`, one CUDA launch sequence), the ranks sum those partials with one
-collective, and the result is cast to bf16 once (`cast_bf16`), so the output is the
-single-GPU layer's output up to the order of one fp32 addition per rank.
+(`kernel_fn_partial`, one CUDA launch sequence), the ranks' partials are summed in fp32 and
+cast to bf16 once, so the output is the single-GPU layer's output up to the order of one fp32
+addition per rank.
 
 Two layouts of the tokens:
-  replicated (decode): every rank holds the same T tokens. Partials [T, H] fp32 are summed
-      with an all-reduce; every rank returns the full output.
+  replicated (decode): every rank holds the same T tokens. Each rank writes its fp32 share
+      [T, H] straight into its own symmetric buffer (mapped into every rank's address space),
+      and one kernel of this library (`muse_moe_peer_allreduce_bf16`) sums the R shares over
+      NVLink in rank order and casts to bf16 -- every rank returns the same bits. (With CPU
+      tensors, as in the gloo tests of the exchange logic, the shares are summed by an
+      all-reduce collective instead.)
   sharded (prefill): rank r holds its own T_r tokens (T_r equal on every rank). Inputs are
       all-gathered (x bf16, ids, weights), every rank computes its experts' share of all
       R * T_r tokens, and a reduce-scatter returns each rank the sum for its own tokens.
 
 Collectives use fixed shapes (no counts sent to the host), so a call issues no host
-synchronisation and can be captured in a CUDA graph together with the NCCL calls.
+synchronisation.
 """
 
 from __future__ import annotations
 
+import ctypes
 from typing import Callable
 
 import torch
@@ -66,6 +71,7 @@ class ExpertParallelMoE:
             n_experts = weights["w13"].shape[0]
         self.n_experts = n_experts
         self.experts = expert_block(n_experts, self.rank, self.world)
+        self.state = None
         if local_fn is None:
             if weights_are_local:
                 state = prepare(weights)
@@ -76,12 +82,53 @@ class ExpertParallelMoE:
             local_fn = lambda d: kernel_fn_partial(d, self.state)  # noqa: E731
         self._local = local_fn
         self._cast = cast_fn or cast_bf16
+        self._peer = None   # symmetric buffers of the decode exchange, set up on first use
+        self._gen = 0
 
     def forward_replicated(self, data: Inputs) -> torch.Tensor:
         """Decode layout: the same T tokens on every rank -> bf16 [T, H] on every rank."""
-        part = self._local(_with_local_range(data, self.experts))
-        dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
-        return self._cast(part)
+        x = data["hidden_states"]
+        local = _with_local_range(data, self.experts)
+        if not x.is_cuda or self.state is None:
+            part = self._local(local)
+            dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
+            return self._cast(part)
+        T, H = x.shape
+        peer = self._peer_buffers(T * H, x.device)
+        self._gen += 1
+        k = self._gen & 1
+        share = peer["buf"][k * peer["cap"]:k * peer["cap"] + T * H].view(T, H)
+        kernel_fn_partial(local, self.state, out=share)
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
+        _lib.call("muse_moe_peer_allreduce_bf16", peer["shares"][k], peer["flags"], self.world, self.rank,
+                  self._gen, T * H, out.data_ptr(), torch.cuda.current_stream(x.device).cuda_stream)
+        return out
+
+    def _peer_buffers(self, numel: int, device) -> dict:
+        """Symmetric buffer [2 shares of cap floats | flags] of every rank, mapped into this one
+        (collective: every rank calls it with the same numel on its first decode call, and again
+        when a call needs more room)."""
+        if self._peer is not None and numel <= self._peer["cap"]:
+            return self._peer
+        import torch.distributed._symmetric_memory as symm
+        if self._peer is not None:   # growing: no rank may still be reading the old buffers
+            torch.cuda.synchronize(device)
+            dist.barrier(group=self.group)
+        cap = (max(numel, 1 << 16) + 63) // 64 * 64        # floats; keeps the shares 256-byte aligned
+        buf = symm.empty(2 * cap + 64, dtype=torch.float32, device=device)
+        buf[2 * cap:].zero_()                                # flag slots start at 0 (generation counts from 1)
+        torch.cuda.synchronize(device)
+        handle = symm.rendezvous(buf, self.group if self.group is not None else dist.group.WORLD)
+        bases = [int(p) for p in handle.buffer_ptrs]
+        u64 = ctypes.c_uint64 * self.world
+        self._peer = {
+            "buf": buf, "handle": handle, "cap": cap,
+            "shares": [u64(*[b + k * cap * 4 for b in bases]) for k in (0, 1)],
+            "flags": u64(*[b + 2 * cap * 4 for b in bases]),
+        }
+        self._gen = 0
+        dist.barrier(group=self.group)                       # every rank's flags are zero before use
+        return self._peer
 
     def forward_sharded(self, data: Inputs) -> torch.Tensor:
         """Prefill layout: this rank's T_r tokens (T_r equal on every rank) -> bf16 [T_r, H],

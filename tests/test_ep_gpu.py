@@ -1,5 +1,6 @@
-"""Expert parallelism on 2+ GPUs of one node (NCCL): every rank's output against the oracle
-over all experts. Skipped with fewer than two GPUs."""
+"""Expert parallelism on 2+ GPUs of one node: the decode exchange over NVLink peer memory and
+the prefill exchange on NCCL, every rank's output against the oracle over all experts.
+Skipped with fewer than two GPUs."""
 
 from __future__ import annotations
 
@@ -54,6 +55,9 @@ def _rank_main(rank, world, port, T, result_dir):
         d = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in d.items()}
         moe = ep.ExpertParallelMoE(w)
         rep = moe.forward_replicated(d)
+        for _ in range(2):   # both share buffers (generation parity) and a fresh generation
+            again = moe.forward_replicated(d)
+            assert torch.equal(again.view(torch.int16), rep.view(torch.int16))
         t_r = T // world
         sl = slice(rank * t_r, (rank + 1) * t_r)
         shard = moe.forward_sharded({**d, "hidden_states": d["hidden_states"][sl],
@@ -84,9 +88,12 @@ def test_expert_parallel_matches_oracle(pkg, tmp_path, T):
     synth, shape = _shape()
     d = synth.baseline_input(shape, T, seed=T)
     ref = oracle_out(d, to_numpy_weights(synth.baseline_weights(shape, seed=3)))
+    rep0 = np.load(tmp_path / "rep0.npy")
     for r in range(world):
-        ok, msg, _, _ = orc.compare(np.load(tmp_path / f"rep{r}.npy"), ref, TOL)
+        got = np.load(tmp_path / f"rep{r}.npy")
+        ok, msg, _, _ = orc.compare(got, ref, TOL)
         assert ok, f"rank {r} replicated: {msg}"
+        np.testing.assert_array_equal(got, rep0)   # every rank sums the shares in rank order
     T_used = (T // world) * world
     got = np.concatenate([np.load(tmp_path / f"shard{r}.npy") for r in range(world)])
     ok, msg, _, _ = orc.compare(got, ref[:T_used], TOL)
