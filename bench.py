@@ -12,8 +12,9 @@ replay of kernel_fn, preceded (outside its timing) by a 512 MiB write that flush
 and timed with CUDA events on the launching stream. `value` is the geometric mean over the
 sweep of the mean us/call; `per_T` lists each token count. Under torchrun (N > 1) the layer
 runs expert-parallel: each rank holds E/N experts, every rank sees all tokens (the decode
-layout), the fp32 shares are all-reduced over NCCL inside the captured graph, and times are the
-max over ranks (strong scaling: the same call, split N ways).
+layout), the fp32 shares are summed over NVLink peer memory by the library's own kernel inside
+the captured graphs, and times are the max over ranks (strong scaling: the same call, split N
+ways).
 
 `--impl reference` times the CPU oracle (the reference's fp32 dequantise-then-accumulate
 path restated in numpy, all host cores) on the same workload; rank 0 only.
@@ -228,7 +229,7 @@ def config_block(args, shape, tokens):
             "weights": "NVFP4 (e2m1, e4m3 block-16 scales, fp32 global scale) from N(0,0.02)",
             "activations": "bf16 N(0,1)", "l2": "flushed by a 512 MiB write before every timed call",
             "parallelism": (f"ep{args.gpus}: experts split in contiguous blocks, tokens replicated, "
-                            "fp32 shares all-reduced over NCCL") if args.gpus > 1 else "single GPU"}
+                            "fp32 shares summed over NVLink peer memory") if args.gpus > 1 else "single GPU"}
 
 
 # ----------------------------------------------------------------------------- CPU baseline leg
@@ -275,6 +276,7 @@ def run_muse(args, world, rank, local):
         # rank holds all tokens (decode layout) and the fp32 shares are all-reduced over NCCL
         from muse_moe_w4a16_b200 import ep
         moe = ep.ExpertParallelMoE(w)
+        moe.reserve_decode(max(tokens), shape.hidden, dev)   # before any graph is captured
         layer_call = moe.forward_replicated
         experts = moe.experts
     else:
@@ -285,9 +287,8 @@ def run_muse(args, world, rank, local):
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
-    # Device-resident inputs and one captured graph per token count. With N > 1 the calls
-    # contain NCCL collectives, which stay out of graphs: they are launched eagerly (the flush
-    # in front of each call keeps the GPU behind the host, so launch gaps do not show).
+    # Device-resident inputs and one captured graph per token count (with N > 1 a pair of
+    # graphs, one per exchange-buffer parity: the decode call holds no collective library call).
     graphs, outs, dev_in = {}, {}, {}
     for t in tokens:
         d = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in inputs[t].items()}
@@ -299,7 +300,7 @@ def run_muse(args, world, rank, local):
             with torch.cuda.graph(g):
                 outs[t] = layer_call(d)
         else:
-            g = _Eager(lambda d=d: layer_call(d))
+            g = moe.decode_graphs(d)
         graphs[t] = g
 
     # End-to-end: pinned host inputs -> device, layer call, result -> pinned host. One graph
@@ -436,8 +437,8 @@ def run_muse(args, world, rank, local):
         # whole expert-parallel call: every rank's algorithmic bytes over the slowest rank's
         # time, against N GPUs' bandwidth
         achieved = sum(r["bytes"] for r in per_rows) / (sum(per_t) * 1e-6) / 1e9
-        roof_kernel = (f"whole expert-parallel layer call over {world} GPUs (local GEMMs + combine + "
-                       f"NCCL all-reduce + cast), sweep aggregate, against {world} x HBM peak")
+        roof_kernel = (f"whole expert-parallel layer call over {world} GPUs (local layer kernels + "
+                       f"peer-memory exchange), sweep aggregate, against {world} x HBM peak")
         roof_peak = pk["hbm_gbs"] * world
     line = {
         "metric": metric_name(args), "value": round(geomean(per_t), 3), "unit": "us/call",
@@ -461,7 +462,7 @@ def run_muse(args, world, rank, local):
         line["cpu_baseline"] = cpu_baseline(shape, tokens, w, inputs)
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del graphs   # graphs holding NCCL calls go before the process group
+    del graphs   # graphs go before the process group
     torch.cuda.synchronize()
     return 0
 

@@ -144,17 +144,20 @@ int muse_moe_cast_bf16(const float* in, void* out, size_t n, muse_stream_t strea
 
 /*
  * The decode-layout exchange of an expert-parallel layer over NVLink peer memory:
- * out (bf16 [n], this rank) = sum over ranks r = 0 .. ranks-1, in that order, of shares[r]
- * (fp32 [n] each, the ranks' muse_moe_forward_partial outputs). shares[r] and flags[r] are
+ * out (bf16 [n], this rank) = sum over ranks r = 0 .. ranks-1, in that order, of rank r's share
+ * (fp32 [n], its muse_moe_forward_partial output). shares0[r] / shares1[r] are rank r's two
+ * share buffers and flags[r] its flag array (16 uint32, zero before the first call), all as
  * device addresses valid on this GPU (peer mappings of every rank's symmetric buffers, this
- * rank's own included); flags[r] is rank r's array of 8 uint32 slots, zero before the first
- * call. Every rank calls it with the same gen = 1, 2, 3, ... and alternates its share buffer
- * by gen parity. Waits for the peers are bounded (~1 s); on expiry the output is left
- * untouched and muse_moe_device_status reports 6. Replaces the all-reduce that sums the ep8
- * ranks' partial outputs (reference.py:18-22, TASK.md:29 run one rank per GPU).
+ * rank's own included). The call's generation g = 1, 2, 3, ... is counted on the device (so a
+ * captured graph stays valid); call g reads the buffers of parity g & 1, so the caller writes
+ * its share of the g-th call into shares{g & 1}[rank]. Waits for the peers are bounded (~1 s);
+ * on expiry the output is left untouched and muse_moe_device_status reports 6. Replaces the
+ * all-reduce that sums the ep8 ranks' partial outputs (reference.py:18-22, TASK.md:29 run one
+ * rank per GPU).
  */
-int muse_moe_peer_allreduce_bf16(const uint64_t* shares, const uint64_t* flags, int ranks, int rank,
-                                 uint32_t gen, size_t n, void* out, muse_stream_t stream);
+int muse_moe_peer_allreduce_bf16(const uint64_t* shares0, const uint64_t* shares1,
+                                 const uint64_t* flags, int ranks, int rank, size_t n, void* out,
+                                 muse_stream_t stream);
 
 /*
  * muse_moe_forward, with five caller-created CUDA events (cudaEvent_t, passed as void*)

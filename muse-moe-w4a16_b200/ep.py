@@ -93,16 +93,32 @@ class ExpertParallelMoE:
             part = self._local(local)
             dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
             return self._cast(part)
-        T, H = x.shape
-        peer = self._peer_buffers(T * H, x.device)
+        self._peer_buffers(x.shape[0] * x.shape[1], x.device)
         self._gen += 1
-        k = self._gen & 1
-        share = peer["buf"][k * peer["cap"]:k * peer["cap"] + T * H].view(T, H)
+        return self._decode(local, self._gen & 1)
+
+    def _decode(self, local: Inputs, parity: int) -> torch.Tensor:
+        """The rank's share written into its share buffer `parity`, then the peer exchange (the
+        kernel takes the generation, and so the parity it reads, from the device)."""
+        x = local["hidden_states"]
+        T, H = x.shape
+        peer = self._peer
+        share = peer["buf"][parity * peer["cap"]:parity * peer["cap"] + T * H].view(T, H)
         kernel_fn_partial(local, self.state, out=share)
         out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
-        _lib.call("muse_moe_peer_allreduce_bf16", peer["shares"][k], peer["flags"], self.world, self.rank,
-                  self._gen, T * H, out.data_ptr(), torch.cuda.current_stream(x.device).cuda_stream)
+        _lib.call("muse_moe_peer_allreduce_bf16", peer["shares"][0], peer["shares"][1], peer["flags"],
+                  self.world, self.rank, T * H, out.data_ptr(), torch.cuda.current_stream(x.device).cuda_stream)
         return out
+
+    def decode_graphs(self, data: Inputs) -> "DecodeGraphs":
+        """CUDA graphs of the decode call for these (device) inputs; see DecodeGraphs."""
+        return DecodeGraphs(self, data)
+
+    def reserve_decode(self, tokens: int, hidden: int, device) -> None:
+        """Size the decode exchange buffers for batches of up to `tokens` (collective). Graphs
+        captured before a batch grows the buffers would point at released memory, so reserve
+        the largest batch before capturing any."""
+        self._peer_buffers(tokens * hidden, device)
 
     def _peer_buffers(self, numel: int, device) -> dict:
         """Symmetric buffer [2 shares of cap floats | flags] of every rank, mapped into this one
@@ -116,7 +132,7 @@ class ExpertParallelMoE:
             dist.barrier(group=self.group)
         cap = (max(numel, 1 << 16) + 63) // 64 * 64        # floats; keeps the shares 256-byte aligned
         buf = symm.empty(2 * cap + 64, dtype=torch.float32, device=device)
-        buf[2 * cap:].zero_()                                # flag slots start at 0 (generation counts from 1)
+        buf[2 * cap:].zero_()                                # flags and the generation counter start at 0
         torch.cuda.synchronize(device)
         handle = symm.rendezvous(buf, self.group if self.group is not None else dist.group.WORLD)
         bases = [int(p) for p in handle.buffer_ptrs]
@@ -148,3 +164,32 @@ class ExpertParallelMoE:
         mine = torch.empty((t_r, part.shape[1]), dtype=part.dtype, device=part.device)
         dist.reduce_scatter_tensor(mine, part, op=dist.ReduceOp.SUM, group=self.group)
         return self._cast(mine)
+
+
+class DecodeGraphs:
+    """Two CUDA graphs of one rank's decode call (share buffer parity 0 and 1) for fixed input
+    tensors; replay() runs the one the next generation needs and returns its output tensor.
+    The generation itself is counted on the device, so every rank must replay (or call
+    forward_replicated) in the same sequence. Holds no collective library call."""
+
+    def __init__(self, moe: ExpertParallelMoE, data: Inputs):
+        x = data["hidden_states"]
+        moe._peer_buffers(x.shape[0] * x.shape[1], x.device)
+        self.moe = moe
+        self.buf = moe._peer["buf"]
+        local = _with_local_range(data, moe.experts)
+        self.graphs, self.outs = [], []
+        for parity in (0, 1):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                self.outs.append(moe._decode(local, parity))
+            self.graphs.append(g)
+
+    def replay(self) -> torch.Tensor:
+        if self.moe._peer is None or self.moe._peer["buf"] is not self.buf:
+            raise _lib.MuseError(_lib.MUSE_ERR_INVALID_ARGUMENT,
+                                 "the decode buffers were reallocated after this capture (reserve_decode first)")
+        self.moe._gen += 1
+        k = self.moe._gen & 1
+        self.graphs[k].replay()
+        return self.outs[k]

@@ -119,3 +119,19 @@ def test_profiled_forward_rejects_missing_events(lib):
     args = [None] * 3 + [1, 2, 0, 8, 256, 256] + [None] * 9 + [0, None]
     assert lib.muse_moe_forward_profiled(*args, None) == _lib.MUSE_ERR_INVALID_ARGUMENT
     assert lib.muse_moe_forward_profiled(*args, ev) == _lib.MUSE_ERR_INVALID_ARGUMENT
+
+
+def test_peer_allreduce_rejects_bad_arguments(lib):
+    """Argument checks of the expert-parallel exchange run before any device work."""
+    from muse_moe_w4a16_b200 import _lib
+    u64 = ctypes.c_uint64 * 2
+    s0, s1, flags = u64(0x1000, 0x2000), u64(0x1100, 0x2100), u64(0x3000, 0x4000)
+    f = lib.muse_moe_peer_allreduce_bf16
+    bad = _lib.MUSE_ERR_INVALID_ARGUMENT
+    out = ctypes.c_void_p(0x5000)
+    assert f(s0, s1, flags, 2, 2, 64, out, None) == bad                 # rank out of range
+    assert f(s0, s1, flags, 9, 0, 64, out, None) == bad                 # more than 8 ranks
+    assert f(s0, s1, flags, 2, 0, 60, out, None) == bad                 # n not a multiple of 8
+    assert f(s0, s1, flags, 2, 0, 64, None, None) == bad                # no output
+    assert f(u64(0x1000, 0), s1, flags, 2, 0, 64, out, None) == bad     # null peer share
+    assert f(u64(0x1004, 0x2000), s1, flags, 2, 0, 64, out, None) == bad  # misaligned share

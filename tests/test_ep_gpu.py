@@ -58,6 +58,13 @@ def _rank_main(rank, world, port, T, result_dir):
         for _ in range(2):   # both share buffers (generation parity) and a fresh generation
             again = moe.forward_replicated(d)
             assert torch.equal(again.view(torch.int16), rep.view(torch.int16))
+        graphs = moe.decode_graphs(d)   # captured decode calls, replayed in parity order
+        for _ in range(3):
+            got = graphs.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(got.view(torch.int16), rep.view(torch.int16))
+        again = moe.forward_replicated(d)   # eager calls and replays share the generation count
+        assert torch.equal(again.view(torch.int16), rep.view(torch.int16))
         t_r = T // world
         sl = slice(rank * t_r, (rank + 1) * t_r)
         shard = moe.forward_sharded({**d, "hidden_states": d["hidden_states"][sl],
