@@ -22,9 +22,56 @@ __host__ __device__ constexpr int route_scratch_ints(int threads) {
 // __match_any_sync). Chunks go in order, so the scatter is stable. Writes offsets[n_local+1],
 // pair_order[n_pairs] (tail -1) and, when non-null, pair_row[n_pairs] (-1 for non-local).
 // Ends with __syncthreads().
+// Small lists (n_pairs <= kRouteDirectMax, blockDim.x > n_local): thread i places pair i directly --
+// its position is (pairs of smaller local expert) + (pairs of its expert with smaller flat
+// index), both counted over the list in shared memory -- one pass instead of a histogram,
+// scan and per-warp scatter. Same output as the general path.
+constexpr int kRouteDirectMax = 128;
+
+__device__ inline void route_block_direct(const int32_t* __restrict__ ids, int n_pairs, int lo,
+                                          int n_local, int* scratch, int32_t* offsets,
+                                          int32_t* pair_order, int32_t* pair_row) {
+  int* le = scratch;  // [n_pairs] local expert of each pair, or -1
+  const int tid = threadIdx.x;
+  if (tid < n_pairs) {
+    const int e = ids[tid] - lo;
+    le[tid] = (unsigned)e < (unsigned)n_local ? e : -1;
+  }
+  __syncthreads();
+  int total = 0;  // local pairs (every thread counts them; used for the tail below)
+  if (tid < n_pairs) {
+    const int e = le[tid];
+    int before = 0, rank = 0;
+    for (int j = 0; j < n_pairs; ++j) {
+      const int ej = le[j];
+      total += ej >= 0;
+      before += (unsigned)ej < (unsigned)e;  // 0 <= ej < e
+      rank += (ej == e) & (j < tid);
+    }
+    if (e >= 0) {
+      pair_order[before + rank] = tid;
+      if (pair_row) pair_row[tid] = before + rank;
+    } else {
+      if (pair_row) pair_row[tid] = -1;
+    }
+    if (tid >= total) pair_order[tid] = -1;  // unused tail
+  }
+  if (tid <= n_local) {  // offsets[e] = local pairs of experts below e
+    int c = 0;
+    for (int j = 0; j < n_pairs; ++j) c += (unsigned)le[j] < (unsigned)tid;
+    offsets[tid] = c;
+  }
+  __syncthreads();
+}
+
 __device__ inline void route_block(const int32_t* __restrict__ ids, int n_pairs, int lo, int n_local,
                                    int* scratch, int32_t* offsets, int32_t* pair_order,
                                    int32_t* pair_row) {
+  // (the pass costs every thread O(n_pairs); at 256 pairs it is no faster than the general path)
+  if (n_pairs <= kRouteDirectMax && (int)blockDim.x >= kRouteDirectMax && (int)blockDim.x > n_local) {
+    route_block_direct(ids, n_pairs, lo, n_local, scratch, offsets, pair_order, pair_row);
+    return;
+  }
   int* hist = scratch;
   int* base = hist + kMaxLocalExperts;
   int* wsum = base + kMaxLocalExperts;
