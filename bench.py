@@ -169,6 +169,33 @@ def input_seed(workload_name: str, t: int) -> int:
     return 1000 * int(workload_name.removeprefix("cfg") or 0) + t
 
 
+# The reference's own problem (cfg0: E=256, top-8, H=I=4096, 32 local experts, the reference's
+# generators) is the one shape with published numbers: the reference's best H200 run per shape
+# (README.md:13-18), keyed by batch size: decode-1/16/32 and verify-8/128/256.
+PUBLISHED_US = {"cfg0": {1: 47.5, 16: 120.3, 32: 154.8, 8: 96.8, 128: 246.7, 256: 327.6}}
+
+
+def make_weights(synth, shape, device):
+    if shape.router.startswith("reference"):
+        return synth.reference_weights(shape, seed=synth.WEIGHTS_SEED, device=device)
+    return synth.baseline_weights(shape, seed=synth.WEIGHTS_SEED, device=device)
+
+
+def make_input(synth, shape, workload_name: str, t: int):
+    if shape.router.startswith("reference"):
+        dist = shape.router.split("-", 1)[1] if "-" in shape.router else "normal"
+        return synth.reference_input(shape, t, seed=input_seed(workload_name, t), dist=dist)
+    return synth.baseline_input(shape, t, seed=input_seed(workload_name, t))
+
+
+def published_ratio(args, tokens, value):
+    """value / the published geomean over the same token counts, when the workload has one."""
+    pub = PUBLISHED_US.get(args.workload)
+    if not pub or any(t not in pub for t in tokens):
+        return None
+    return round(value / geomean([pub[t] for t in tokens]), 4)
+
+
 # ----------------------------------------------------------------------------- reference arm
 
 def run_reference(args, world, rank):
@@ -180,11 +207,11 @@ def run_reference(args, world, rank):
     from muse_moe_w4a16_b200 import synth
     shape, tokens = workload(args, synth)
     cores = os.cpu_count() or 1
-    w = synth.baseline_weights(shape, seed=synth.WEIGHTS_SEED, device="cuda" if torch.cuda.is_available() else "cpu")
+    w = make_weights(synth, shape, "cuda" if torch.cuda.is_available() else "cpu")
     w_np = {k: (v.view(torch.uint8) if v.dtype == torch.float8_e4m3fn else
                 v.view(torch.uint16) if v.dtype == torch.bfloat16 else v).cpu().numpy() for k, v in w.items()}
     del pkg
-    inputs = {t: synth.baseline_input(shape, t, seed=input_seed(args.workload, t)) for t in tokens}
+    inputs = {t: make_input(synth, shape, args.workload, t) for t in tokens}
 
     def call(t):
         d = inputs[t]
@@ -226,7 +253,10 @@ def config_block(args, shape, tokens):
     return {"workload": f"{args.workload}: E={shape.n_experts} top-{shape.top_k} H={shape.hidden} "
                         f"I={shape.inter} local=[{shape.local_start},{shape.local_start + shape.n_local}) "
                         f"router={shape.router} T={list(tokens)}",
-            "weights": "NVFP4 (e2m1, e4m3 block-16 scales, fp32 global scale) from N(0,0.02)",
+            "weights": ("NVFP4 from the reference's generators (log-normal e4m3 block scales, "
+                        "Student-t expert popularity, busiest-rank rotation)"
+                        if shape.router.startswith("reference") else
+                        "NVFP4 (e2m1, e4m3 block-16 scales, fp32 global scale) from N(0,0.02)"),
             "activations": "bf16 N(0,1)", "l2": "flushed by a 512 MiB write before every timed call",
             "parallelism": (f"ep{args.gpus}: experts split in contiguous blocks, tokens replicated, "
                             "fp32 shares summed over NVLink peer memory") if args.gpus > 1 else "single GPU"}
@@ -270,7 +300,7 @@ def run_muse(args, world, rank, local):
 
     dev = torch.device("cuda", local)
     shape, tokens = workload(args, synth)
-    w = synth.baseline_weights(shape, seed=synth.WEIGHTS_SEED, device=dev)
+    w = make_weights(synth, shape, dev)
     if world > 1:
         # expert-parallel: this rank repacks and computes only its block of experts; every
         # rank holds all tokens (decode layout) and the fp32 shares are all-reduced over NCCL
@@ -283,7 +313,7 @@ def run_muse(args, world, rank, local):
         state = pkg.prepare(w)
         layer_call = lambda d: pkg.kernel_fn(d, state)  # noqa: E731
         experts = range(shape.local_start, shape.local_start + shape.n_local)
-    inputs = {t: synth.baseline_input(shape, t, seed=input_seed(args.workload, t)) for t in tokens}
+    inputs = {t: make_input(synth, shape, args.workload, t) for t in tokens}
     flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
 
@@ -445,7 +475,8 @@ def run_muse(args, world, rank, local):
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(sum(per_t) / 1e3, 5), "higher_is_better": False,
         "scaling": "strong" if world > 1 else "weak",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; random-init NVFP4 weights)",
+        "vs_baseline": published_ratio(args, tokens, geomean(per_t)), "dtype": "bf16",
+        "data": "synthetic (seeded; random-init NVFP4 weights)",
         "config": config_block(args, shape, tokens),
         "per_T": per_rows,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": roof_peak, "unit": "GB/s",
