@@ -5,6 +5,7 @@
 // zeros. Slots are summed in ascending expert order, the order ref_kernel's index_add_ uses.
 // The sum of squares of a pair is added up from its H/32 slice sums in a fixed order, so the
 // result does not depend on how the GEMM's CTAs were scheduled.
+#include "combine.cuh"
 #include "common.cuh"
 #include "kernels.cuh"
 
@@ -12,77 +13,41 @@ namespace muse {
 
 namespace {
 
-constexpr int kThreads = 128;
+constexpr int kThreads = 256;
 constexpr int kColsPerCta = kThreads * 4;
 
-// grid (tokens, ceil(H / 512)). Warp w reduces the slice sums of slots w, w + 4, ...
+// grid (tokens, ceil(H / 1024)). Warp w computes the coefficients of slots w, w + 8, ...
 // kF32Out: write the fp32 sum (an expert-parallel rank's partial) instead of bf16.
 template <bool kF32Out>
 __global__ void __launch_bounds__(kThreads)
 combine_kernel(const int32_t* __restrict__ ids, const float* __restrict__ topk_weights,
                const int32_t* __restrict__ pair_row, const float* __restrict__ ypart,
                const float* __restrict__ ssq, int top_k, int H, void* __restrict__ out) {
-  __shared__ int s_row[kMaxTopK], s_key[kMaxTopK];
-  __shared__ float s_coef[kMaxTopK];
-  __shared__ int s_order[kMaxTopK];
+  __shared__ int s_row[kMaxTopK], s_key[kMaxTopK], s_order[kMaxTopK], s_srow[kMaxTopK];
+  __shared__ float s_coef[kMaxTopK], s_scoef[kMaxTopK];
   __shared__ int s_n;
   const int t = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int parts = H >> 5;
   for (int s = warp; s < top_k; s += kThreads / 32) {
     const int p = pair_row[t * top_k + s];
-    float sum = 0.f;
-    if (p >= 0) {
-      const float* src = ssq + (size_t)p * parts;
-      for (int j = lane; j < parts; j += 32) sum += src[j];
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-    }
+    float coef = 0.f;
+    if (p >= 0) coef = post_norm_coef(ssq + (size_t)p * (H >> 5), H, topk_weights[t * top_k + s]);
     if (lane == 0) {
       s_row[s] = p;
       s_key[s] = ids[t * top_k + s];
-      s_coef[s] = p >= 0 ? topk_weights[t * top_k + s] * rsqrtf(sum / (float)H + kPostNormEps) : 0.f;
+      s_coef[s] = coef;
     }
   }
   __syncthreads();
-  if (tid == 0) {
-    // local slots in ascending expert id (insertion sort over <= 16 entries)
-    int n = 0;
-    for (int s = 0; s < top_k; ++s) {
-      if (s_row[s] < 0) continue;
-      int j = n++;
-      while (j > 0 && s_key[s_order[j - 1]] > s_key[s]) {
-        s_order[j] = s_order[j - 1];
-        --j;
-      }
-      s_order[j] = s;
-    }
-    s_n = n;
-  }
+  if (tid == 0) s_n = sort_local_slots(s_row, s_key, s_coef, top_k, s_order, s_srow, s_scoef);
   __syncthreads();
-  const int n = s_n;
   const int h4 = blockIdx.y * kThreads + tid;  // float4 column group
   if (h4 * 4 >= H) return;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int j = 0; j < n; ++j) {
-    const int s = s_order[j];
-    const float4 v = reinterpret_cast<const float4*>(ypart + (size_t)s_row[s] * H)[h4];
-    const float c = s_coef[s];
-    acc.x = fmaf(c, v.x, acc.x);
-    acc.y = fmaf(c, v.y, acc.y);
-    acc.z = fmaf(c, v.z, acc.z);
-    acc.w = fmaf(c, v.w, acc.w);
-  }
-  if (kF32Out) {
+  const float4 acc = weighted_rows(ypart, H, s_srow, s_scoef, s_n, h4);
+  if (kF32Out)
     reinterpret_cast<float4*>(static_cast<float*>(out) + (size_t)t * H)[h4] = acc;
-  } else {
-    __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
-    __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
-    uint2 packed;
-    packed.x = *reinterpret_cast<uint32_t*>(&lo);
-    packed.y = *reinterpret_cast<uint32_t*>(&hi);
-    reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + (size_t)t * H)[h4] = packed;
-  }
+  else
+    reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + (size_t)t * H)[h4] = pack_bf16x4(acc);
 }
 
 // out[i] = bf16(in[i]), 8 elements per thread (n a multiple of 8).

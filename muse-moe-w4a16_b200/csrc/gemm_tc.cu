@@ -27,6 +27,7 @@
 // 64 columns (128 K elements as bf16 pairs) followed by n_acc accumulators of n_box columns.
 // Every mbarrier wait is bounded; on timeout the CTA records an error flag and unwinds.
 #include "common.cuh"
+#include "combine.cuh"
 #include "kernels.cuh"
 #include "layout.cuh"
 #include "ptx.cuh"
@@ -86,8 +87,8 @@ struct SharedCtl {
   int offs[kMaxExperts + 1];         // route_inline: expert ranges of the pair rows
   int order[kMaxInlinePairs];        // route_inline: token of each expert-grouped pair row
   uint8_t slot_of_row[kMaxInlinePairs];  // route_inline: top-k slot of each pair row
-  int c_row[kMaxTopK], c_key[kMaxTopK], c_order[kMaxTopK], c_n;  // combine of one token
-  float c_coef[kMaxTopK];
+  int c_row[kMaxTopK], c_key[kMaxTopK], c_order[kMaxTopK], c_srow[kMaxTopK], c_n;  // combine of one token
+  float c_coef[kMaxTopK], c_scoef[kMaxTopK];
 };
 
 // Per-launch geometry shared by all roles.
@@ -182,9 +183,9 @@ __device__ __forceinline__ void record_error(int* flag, int code) {
 // The layer's combine for the tokens of this CTA (fused launches): out[t] = sum over t's local
 // slots, in ascending expert order, of topk_weight * rsqrt(mean(ypart^2) + eps) * ypart, fp32,
 // then bf16 (or fp32 for an expert-parallel share). Rows are waited for through the GEMM2
-// tile counters. Restates reference.py:88-90,106-107 like combine.cu.
+// tile counters. Restates reference.py:88-90,106-107 with combine.cu's arithmetic.
 __device__ __forceinline__ void combine_tokens(SharedCtl& ctl, const GemmArgs& a, int n_local, int n_box) {
-  const int K = a.top_k, H = a.hidden, parts = H >> 5;
+  const int K = a.top_k, H = a.hidden;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total_rows = ctl.offs[n_local];
   for (int t = blockIdx.x; t < a.tokens; t += gridDim.x) {
@@ -208,11 +209,7 @@ __device__ __forceinline__ void combine_tokens(SharedCtl& ctl, const GemmArgs& a
                                                                                  a.combine_target)
                                                              : true);
         if (!ready && lane == 0) record_error(a.error_flag, 5);
-        float sum = 0.f;
-        for (int j = lane; j < parts; j += 32) sum += __ldcg(a.ssq + (size_t)r * parts + j);
-#pragma unroll
-        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-        coef = a.topk_weights[t * K + sl] * rsqrtf(sum / (float)H + kPostNormEps);
+        coef = post_norm_coef(a.ssq + (size_t)r * (H >> 5), H, a.topk_weights[t * K + sl]);
       }
       if (lane == 0) {
         ctl.c_coef[sl] = coef;
@@ -220,42 +217,16 @@ __device__ __forceinline__ void combine_tokens(SharedCtl& ctl, const GemmArgs& a
       }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {  // local slots in ascending expert id
-      int n = 0;
-      for (int sl = 0; sl < K; ++sl) {
-        if (ctl.c_row[sl] < 0) continue;
-        int j = n++;
-        while (j > 0 && ctl.c_key[ctl.c_order[j - 1]] > ctl.c_key[sl]) {
-          ctl.c_order[j] = ctl.c_order[j - 1];
-          --j;
-        }
-        ctl.c_order[j] = sl;
-      }
-      ctl.c_n = n;
-    }
+    if (threadIdx.x == 0)
+      ctl.c_n = sort_local_slots(ctl.c_row, ctl.c_key, ctl.c_coef, K, ctl.c_order, ctl.c_srow, ctl.c_scoef);
     __syncthreads();
     const int n = ctl.c_n;
     for (int h4 = threadIdx.x; h4 * 4 < H; h4 += blockDim.x) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int j = 0; j < n; ++j) {
-        const int sl = ctl.c_order[j];
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(a.ypart + (size_t)ctl.c_row[sl] * H) + h4);
-        const float c = ctl.c_coef[sl];
-        acc.x = fmaf(c, v.x, acc.x);
-        acc.y = fmaf(c, v.y, acc.y);
-        acc.z = fmaf(c, v.z, acc.z);
-        acc.w = fmaf(c, v.w, acc.w);
-      }
-      if (a.out_f32) {
+      const float4 acc = weighted_rows(a.ypart, H, ctl.c_srow, ctl.c_scoef, n, h4);
+      if (a.out_f32)
         reinterpret_cast<float4*>(static_cast<float*>(a.out) + (size_t)t * H)[h4] = acc;
-      } else {
-        __nv_bfloat162 lo2 = __floats2bfloat162_rn(acc.x, acc.y);
-        __nv_bfloat162 hi2 = __floats2bfloat162_rn(acc.z, acc.w);
-        uint2 packed;
-        packed.x = *reinterpret_cast<uint32_t*>(&lo2);
-        packed.y = *reinterpret_cast<uint32_t*>(&hi2);
-        reinterpret_cast<uint2*>(static_cast<uint16_t*>(a.out) + (size_t)t * H)[h4] = packed;
-      }
+      else
+        reinterpret_cast<uint2*>(static_cast<uint16_t*>(a.out) + (size_t)t * H)[h4] = pack_bf16x4(acc);
     }
     __syncthreads();
   }
@@ -381,11 +352,17 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
   // and the epilogue sums the partial accumulators (rotating with j balances the pipelines
   // when P does not divide the chunk count). Otherwise (few chunks per item) item j goes whole
   // to pipeline j % P, so each item costs one accumulator hand-off instead of P.
+  // A phase is split when the host asks for it (many chunks per item) and also whenever it has
+  // fewer than 4 items per CTA: with 1-2 items a CTA would leave pipelines idle, and splitting
+  // never gives a pipeline more chunks than whole items would, so the CTA's longest pipeline
+  // -- the decode critical path -- gets shorter.
+  const bool split0 = a.ph[0].split_k || (a.ph[0].k_chunks > 1 && n0 < 4 * G);
+  const bool split1 = kFused && a.n_phases > 1 && (a.ph[1].split_k || (a.ph[1].k_chunks > 1 && total - n0 < 4 * G));
   // jm = j % P; returns the first chunk of pipeline p (k_chunks if it has none).
-  auto chunk_begin = [&](int p, int jm, const PhaseArgs& f) {
-    return f.split_k ? (p - jm + kPipes) % kPipes : (p == jm ? 0 : f.k_chunks);
+  auto chunk_begin = [&](int p, int jm, const PhaseArgs& f, bool split) {
+    return split ? (p - jm + kPipes) % kPipes : (p == jm ? 0 : f.k_chunks);
   };
-  auto item_phase = [&](int it) -> const PhaseArgs& { return a.ph[kFused && it >= n0 ? 1 : 0]; };
+  auto phase_of = [&](int it) { return kFused && it >= n0 ? 1 : 0; };
 
   if (warp < kMmaWarp0) {
     // ------------------------------------------------------------------ producers
@@ -405,9 +382,11 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
       int jm = 0;
       for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
         const int it = blockIdx.x + j * G;
-        const PhaseArgs& f = item_phase(it);
-        const int kcn = f.k_chunks, kstep = f.split_k ? kPipes : 1;
-        const int kc0 = chunk_begin(p, jm, f);
+        const int ph = phase_of(it);
+        const PhaseArgs& f = a.ph[ph];
+        const bool split = ph ? split1 : split0;
+        const int kcn = f.k_chunks, kstep = split ? kPipes : 1;
+        const int kc0 = chunk_begin(p, jm, f, split);
         if (kc0 >= kcn) continue;
         const Item t = decode_item(ctl, offs, it, n0, n_local, n_box, mt0, mt1);
         const size_t tile0 = ((size_t)t.e * f.m_tiles + t.m) * kcn;
@@ -520,9 +499,11 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
       uint64_t desc_stage = desc_first;
       int jm = 0;
       for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
-        const PhaseArgs& f = item_phase(blockIdx.x + j * G);
-        const int kcn = f.k_chunks, kstep = f.split_k ? kPipes : 1;
-        const int kc0 = chunk_begin(p, jm, f);
+        const int ph = phase_of(blockIdx.x + j * G);
+        const PhaseArgs& f = a.ph[ph];
+        const bool split = ph ? split1 : split0;
+        const int kcn = f.k_chunks, kstep = split ? kPipes : 1;
+        const int kc0 = chunk_begin(p, jm, f, split);
         if (kc0 >= kcn) continue;
         const int acc = accr.slot;
         if (!__all_sync(0xffffffffu, ptx::mbar_wait_sleep(&pc.acc_empty[acc], accr.phase ^ 1))) {
@@ -590,13 +571,14 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
       const float gs_item = gs_next, pnw_item = pnw_next;
       if (blockIdx.x + (j + 1) * G < total) item_consts(blockIdx.x + (j + 1) * G, t_next, gs_next, pnw_next);
       const PhaseArgs& f = a.ph[t.ph];
+      const bool split = t.ph ? split1 : split0;
       const int kcn = f.k_chunks;
       // accumulators of the participating pipelines
       uint32_t taddr[kPipes];
       int used = 0;
 #pragma unroll
       for (int p = 0; p < kPipes; ++p) {
-        if (chunk_begin(p, jm, f) >= kcn) continue;
+        if (chunk_begin(p, jm, f, split) >= kcn) continue;
         if (!ptx::mbar_wait_sleep(&ctl.pipe[p].acc_full[accr[p].slot], accr[p].phase)) ok = false;
         taddr[used++] = lane_base + p * kPipeCols + accr[p].slot * n_box;
       }
@@ -671,7 +653,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
       __syncwarp();
 #pragma unroll
       for (int p = 0; p < kPipes; ++p) {
-        if (chunk_begin(p, jm, f) >= kcn) continue;
+        if (chunk_begin(p, jm, f, split) >= kcn) continue;
         if (lane == 0) ptx::mbar_arrive(&ctl.pipe[p].acc_empty[accr[p].slot]);
         accr[p].next(geo.n_acc);
       }
@@ -679,6 +661,9 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     if (!ok && lane == 0) record_error(a.error_flag, 3);
   } else {
     // ------------------------------------------------------------------ dequantisers
+    // Software-pipelined: the codes and scale-table entries of the next chunk are read while
+    // this chunk's tensor-memory stores drain, and the A buffer is waited for only once the
+    // first half of the chunk is converted, so the warp's own latencies overlap its work.
     const int p = (warp - kDeqWarp0) / DW;
     PipeCtl& pc = ctl.pipe[p];
     const int q = warp & 3;                  // TMEM lane quarter
@@ -686,61 +671,76 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     const int row = 32 * q + lane;           // weight row of this thread
     const uint32_t lane_col0 = tbase + ((uint32_t)(32 * q) << 16) + p * kPipeCols;
     const uint32_t m16 = a.mul16, m64 = a.mul64;
+    constexpr int kHalves = DW == 8 ? 1 : 2;  // halves of the chunk this warp converts
     bool ok = true;
     Ring st, ar;
-    int jm = 0;
-    for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
-      const PhaseArgs& f = item_phase(blockIdx.x + j * G);
-      const int kcn = f.k_chunks, kstep = f.split_k ? kPipes : 1;
-      for (int kc = chunk_begin(p, jm, f); kc < kcn; kc += kstep, st.next(Sw), ar.next(geo.n_a)) {
-        const int s = st.slot;
-        const int ab = ar.slot;
-        if (!ptx::mbar_wait_sleep(&pc.w_full[s], st.phase)) {
-          ok = false;
-          break;
-        }
-        // read this row's 64 code bytes and 8 scale bytes, then hand the weight slot back to
-        // the producer before doing any arithmetic
-        const uint8_t* wp = w_slot(p, s);
-        const uint8_t* arow = wp + row * kRowCodeBytes;
-        constexpr int kHalves = DW == 8 ? 1 : 2;  // halves of the chunk this warp converts
-        uint4 cw[2 * kHalves];
-#pragma unroll
-        for (int c = 0; c < 2 * kHalves; ++c)
-          cw[c] = *reinterpret_cast<const uint4*>(arow + 16 * code_slot(row, 2 * hsel + c));
-        const uint2 sfw = *reinterpret_cast<const uint2*>(wp + kTileCodeBytes + row * kRowScaleBytes);
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&pc.w_empty[s]);
-        if (!ptx::mbar_wait_sleep(&pc.a_empty[ab], ar.phase ^ 1)) {
-          ok = false;
-          break;
-        }
-#pragma unroll
-        for (int hh = 0; hh < kHalves; ++hh) {
-          const int half = hsel + hh;
-          const uint4 c0 = cw[2 * hh];
-          const uint4 c1 = cw[2 * hh + 1];
-          const uint32_t sw = half ? sfw.y : sfw.x;  // the 4 scale bytes of these 64 elements
-          const uint32_t sc[4] = {ctl.scale_lut[__byte_perm(sw, 0, 0x4440)],
-                                  ctl.scale_lut[__byte_perm(sw, 0, 0x4441)],
-                                  ctl.scale_lut[__byte_perm(sw, 0, 0x4442)],
-                                  ctl.scale_lut[__byte_perm(sw, 0, 0x4443)]};
-          uint32_t out[32];
-          dequant8(c0.x, sc[0], m16, m64, &out[0]);
-          dequant8(c0.y, sc[0], m16, m64, &out[4]);
-          dequant8(c0.z, sc[1], m16, m64, &out[8]);
-          dequant8(c0.w, sc[1], m16, m64, &out[12]);
-          dequant8(c1.x, sc[2], m16, m64, &out[16]);
-          dequant8(c1.y, sc[2], m16, m64, &out[20]);
-          dequant8(c1.z, sc[3], m16, m64, &out[24]);
-          dequant8(c1.w, sc[3], m16, m64, &out[28]);
-          ptx::tmem_st32(lane_col0 + ab * kACols + half * 32, out);
-        }
-        ptx::tmem_wait_st();
-        ptx::tc_fence_before();
-        __syncwarp();
-        if (lane == 0) ptx::mbar_arrive(&pc.a_full[ab]);
+    // this pipeline's chunks in order: item j (jm = j % P), chunk kc of it
+    int j = -1, jm = kPipes - 1, kc = 0, kcn = 0, kstep = 1;
+    auto advance = [&]() -> bool {
+      kc += kstep;
+      while (kc >= kcn) {
+        ++j;
+        jm = jm + 1 == kPipes ? 0 : jm + 1;
+        if (blockIdx.x + j * G >= total) return false;
+        const int ph = phase_of(blockIdx.x + j * G);
+        const PhaseArgs& f = a.ph[ph];
+        const bool split = ph ? split1 : split0;
+        kcn = f.k_chunks;
+        kstep = split ? kPipes : 1;
+        kc = chunk_begin(p, jm, f, split);
       }
+      return true;
+    };
+    uint4 cw[2 * kHalves];
+    uint32_t sc[4 * kHalves];
+    // Wait for the next weight slot, read this row's code and scale bytes, hand the slot back
+    // to the producer, then look the scales up.
+    auto fetch = [&]() -> bool {
+      if (!ptx::mbar_wait_sleep(&pc.w_full[st.slot], st.phase)) return false;
+      const uint8_t* wp = w_slot(p, st.slot);
+      const uint8_t* arow = wp + row * kRowCodeBytes;
+#pragma unroll
+      for (int c = 0; c < 2 * kHalves; ++c)
+        cw[c] = *reinterpret_cast<const uint4*>(arow + 16 * code_slot(row, 2 * hsel + c));
+      const uint2 sfw = *reinterpret_cast<const uint2*>(wp + kTileCodeBytes + row * kRowScaleBytes);
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&pc.w_empty[st.slot]);
+      st.next(Sw);
+#pragma unroll
+      for (int hh = 0; hh < kHalves; ++hh) {
+        const uint32_t sw = hsel + hh ? sfw.y : sfw.x;  // the 4 scale bytes of these 64 elements
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sc[4 * hh + i] = ctl.scale_lut[__byte_perm(sw, 0, 0x4440 + i)];
+      }
+      return true;
+    };
+    bool more = advance();
+    if (more) ok = fetch();
+    while (ok && more) {
+      const int ab = ar.slot;
+      // 16 columns (32 elements) at a time: column 16 * c4 + 4 * word + pair of this lane
+#pragma unroll
+      for (int c = 0; c < 2 * kHalves; ++c) {
+        uint32_t out[16];
+        const uint4 c4 = cw[c];
+        dequant8(c4.x, sc[2 * c], m16, m64, &out[0]);
+        dequant8(c4.y, sc[2 * c], m16, m64, &out[4]);
+        dequant8(c4.z, sc[2 * c + 1], m16, m64, &out[8]);
+        dequant8(c4.w, sc[2 * c + 1], m16, m64, &out[12]);
+        if (c == 0 && !ptx::mbar_wait_sleep(&pc.a_empty[ab], ar.phase ^ 1)) {
+          ok = false;
+          break;
+        }
+        ptx::tmem_st16(lane_col0 + ab * kACols + hsel * 32 + c * 16, out);
+      }
+      if (!ok) break;
+      more = advance();
+      if (more) ok = fetch();
+      ptx::tmem_wait_st();
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(&pc.a_full[ab]);
+      ar.next(geo.n_a);
     }
     if (!ok && lane == 0) record_error(a.error_flag, 4);
   }
