@@ -661,9 +661,9 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     if (!ok && lane == 0) record_error(a.error_flag, 3);
   } else {
     // ------------------------------------------------------------------ dequantisers
-    // Software-pipelined: the codes and scale-table entries of the next chunk are read while
-    // this chunk's tensor-memory stores drain, and the A buffer is waited for only once the
-    // first half of the chunk is converted, so the warp's own latencies overlap its work.
+    // Each chunk's codes and scale-table entries are read into registers right after the
+    // previous chunk is handed to the MMA, and the A buffer is waited for only once the first
+    // 16 columns are converted.
     const int p = (warp - kDeqWarp0) / DW;
     PipeCtl& pc = ctl.pipe[p];
     const int q = warp & 3;                  // TMEM lane quarter
@@ -734,13 +734,15 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
         ptx::tmem_st16(lane_col0 + ab * kACols + hsel * 32 + c * 16, out);
       }
       if (!ok) break;
-      more = advance();
-      if (more) ok = fetch();
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&pc.a_full[ab]);
       ar.next(geo.n_a);
+      // the next chunk's bytes: read after the hand-off, so the MMA of this chunk never waits
+      // for the next weight tile to land
+      more = advance();
+      if (more) ok = fetch();
     }
     if (!ok && lane == 0) record_error(a.error_flag, 4);
   }
