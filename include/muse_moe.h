@@ -102,6 +102,20 @@ int muse_moe_route(const int32_t* topk_ids, int tokens, int top_k, int local_sta
                    int32_t* pair_row, muse_stream_t stream);
 
 /*
+ * Router top-k, the caller side of the layer: topk_ids / topk_weights for every token from a
+ * row-major fp32 score matrix [tokens, n_experts], on the device (so a model step can stay in
+ * one graph). Replaces the routing of reference.generate_input (reference.py:72-84):
+ * scores.topk(K) -> ids in descending score order (equal scores: lower id first; NaN ranks
+ * above every number, as torch.topk orders it), and
+ *   mode 0: weights = selected scores / their sum          (the reference's renormalisation)
+ *   mode 1: weights = softmax over the K selected scores   (logits -> softmax -> top-K ->
+ *                                                            renormalise, the same values)
+ * top_k <= 16, top_k <= n_experts <= 1024.
+ */
+int muse_moe_router_topk(const float* scores, int tokens, int n_experts, int top_k, int mode,
+                         int32_t* topk_ids, float* topk_weights, muse_stream_t stream);
+
+/*
  * The whole routed-expert layer call: routing, GEMM1 (w13) with SiLU(gate)*up, GEMM2 (w2),
  * post-expert RMSNorm (eps 1e-8) and the top-k-weighted combine, written as bf16 into `out`.
  * Tokens with no local pair get zeros. Replaces kernel_fn (baseline.py:106-151) and computes

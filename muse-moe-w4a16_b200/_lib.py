@@ -24,6 +24,7 @@ SIGNATURES: dict[str, tuple] = {
     "muse_moe_device_status": (_I, [ctypes.POINTER(ctypes.c_int), _I]),
     "muse_moe_prepare_weights": (_I, [_P, _P, _P, _P, _I, _I, _I, _P, _P, _P, _P, _P]),
     "muse_moe_route": (_I, [_P, _I, _I, _I, _I, _P, _P, _P, _P]),
+    "muse_moe_router_topk": (_I, [_P, _I, _I, _I, _I, _P, _P, _P]),
     "muse_moe_forward": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I,
                               _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P]),
     "muse_moe_forward_profiled": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I,

@@ -179,6 +179,28 @@ def cast_bf16(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     return out
 
 
+def route_topk(scores: torch.Tensor, top_k: int, mode: str = "renorm",
+               out: tuple[torch.Tensor, torch.Tensor] | None = None) -> tuple[torch.Tensor, torch.Tensor]:
+    """(topk_ids int32 [T, K], topk_weights fp32 [T, K]) from router scores fp32 [T, E], on the
+    device: the routing step of reference.generate_input (reference.py:72-84), scores.topk(K)
+    then weights = values / values.sum(-1) ("renorm"), or the softmax router's weights, the
+    softmax over the K selected scores ("softmax"). Ids are in descending score order; equal
+    scores keep the lower expert id first."""
+    _require_cuda(scores, "scores")
+    if scores.dtype != torch.float32 or scores.dim() != 2 or not scores.is_contiguous():
+        raise _lib.MuseError(_lib.MUSE_ERR_INVALID_ARGUMENT, "scores must be contiguous fp32 [T, E]")
+    if mode not in ("renorm", "softmax"):
+        raise _lib.MuseError(_lib.MUSE_ERR_INVALID_ARGUMENT, f"unknown router mode {mode!r}")
+    T, E = scores.shape
+    if out is None:
+        out = (torch.empty((T, top_k), dtype=torch.int32, device=scores.device),
+               torch.empty((T, top_k), dtype=torch.float32, device=scores.device))
+    ids, wts = out
+    _lib.call("muse_moe_router_topk", _ptr(scores), T, E, top_k, 0 if mode == "renorm" else 1,
+              _ptr(ids), _ptr(wts), _stream(scores.device))
+    return ids, wts
+
+
 # prepare() results cached per weights dict (never on `data`, TASK.md:75).
 _STATE_CACHE: dict[int, tuple[weakref.ref, dict]] = {}
 

@@ -209,13 +209,12 @@ def _outlier_channels(x, *, generator, frac=0.01, scale=30.0):
     return out
 
 
-def reference_input(shape: MoEShape, tokens: int, seed: int, dist: str = "normal",
-                    rank: str = "busiest", device="cpu"):
-    """Restates reference.generate_input (reference.py:53-85) at any shape: uniform scores plus
-    a Student-t popularity ("normal") or a pow-6 heat and outlier channels ("skewed"), top-K,
-    and the "busiest" rotation that makes the local experts the busiest rank's."""
+def reference_scores(shape: MoEShape, tokens: int, seed: int, dist: str = "normal", device="cpu"):
+    """(x bf16 [T, H], router scores fp32 [T, E]) as reference.generate_input draws them
+    (reference.py:62-71): uniform scores plus a Student-t popularity ("normal") or a pow-6
+    heat and outlier channels ("skewed")."""
     g = torch.Generator(device=device).manual_seed(seed)
-    E, K = shape.n_experts, shape.top_k
+    E = shape.n_experts
     x = torch.randn((tokens, shape.hidden), generator=g, device=device).to(torch.bfloat16)
     scores = torch.rand((tokens, E), generator=g, device=device)
     if dist == "normal":
@@ -226,6 +225,16 @@ def reference_input(shape: MoEShape, tokens: int, seed: int, dist: str = "normal
         heat = torch.rand((E,), generator=g, device=device).pow(6) * 4
         scores = scores + heat
         x = _outlier_channels(x, generator=g)
+    return x, scores
+
+
+def reference_input(shape: MoEShape, tokens: int, seed: int, dist: str = "normal",
+                    rank: str = "busiest", device="cpu"):
+    """Restates reference.generate_input (reference.py:53-85) at any shape: uniform scores plus
+    a Student-t popularity ("normal") or a pow-6 heat and outlier channels ("skewed"), top-K,
+    and the "busiest" rotation that makes the local experts the busiest rank's."""
+    x, scores = reference_scores(shape, tokens, seed, dist, device)
+    E, K = shape.n_experts, shape.top_k
     routed = scores.topk(K, dim=-1)
     count = shape.n_local
     ids = routed.indices

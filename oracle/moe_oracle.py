@@ -116,6 +116,38 @@ def route(topk_ids: np.ndarray, local_start: int, local_count: int):
     return offsets, pair_order, pair_row
 
 
+def router_topk(scores: np.ndarray, top_k: int, mode: str = "renorm"):
+    """The routing step of reference.generate_input (reference.py:72-84): for each token the
+    top_k scores in descending order (equal scores: lower expert id first; NaN above every
+    number, torch.topk's order), ids int32 [T, K], and weights fp32 [T, K]: the selected scores
+    over their sum ("renorm", reference.py:82), or their softmax ("softmax": the synthetic
+    configs' logits -> softmax -> top-K -> renormalise). Sums run in selection order."""
+    s = np.asarray(scores, dtype=np.float32)
+    T, E = s.shape
+    ids = np.zeros((T, top_k), dtype=np.int32)
+    wts = np.zeros((T, top_k), dtype=np.float32)
+    for t in range(T):
+        row = s[t]
+        # sort key: NaN first, then descending value, then ascending id
+        order = sorted(range(E), key=lambda e: (0 if np.isnan(row[e]) else 1,
+                                                0.0 if np.isnan(row[e]) else -float(row[e]), e))
+        sel = order[:top_k]
+        ids[t] = sel
+        v = row[sel].astype(np.float32)
+        if mode == "renorm":
+            total = np.float32(0.0)
+            for x in v:
+                total = np.float32(total + x)
+            wts[t] = v / total
+        else:
+            ex = np.exp((v - v[0]).astype(np.float32)).astype(np.float32)
+            total = np.float32(0.0)
+            for x in ex:
+                total = np.float32(total + x)
+            wts[t] = ex / total
+    return ids, wts
+
+
 def ref_kernel(x_bits, topk_ids, topk_weights, weights: dict, local_start: int, local_count: int,
                d_expert: int, return_f32: bool = False):
     """Restates reference.ref_kernel (reference.py:93-107) for any shape.

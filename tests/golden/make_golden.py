@@ -166,6 +166,27 @@ def main() -> int:
     variants["nan"][1, 2] = float("nan")
     res = {k: bool(ck.compare(v, ref_t, 1.5e-2)[0]) for k, v in variants.items()}
     save("compare_kat", {"results": res}, ref=u16(ref_t), **{k: u16(v) for k, v in variants.items()})
+
+    # ---- 7. router top-k: the reference's own routing step (generate_input, reference.py:72-84,
+    # with a rank other than "busiest" so the ids stay unrotated) on scores drawn as it draws
+    # them (synth.reference_scores, checked against the reference's hidden states), at the
+    # reference problem's E=256, K=8; plus the softmax router of the synthetic configs
+    # (torch softmax -> topk -> renormalise) at E=128, K=8.
+    reference.N_EXPERTS, reference.D_HIDDEN, reference.ROUTED_PER_TOKEN = 256, 128, 8
+    reference.LOCAL = {"ep8": (0, 32)}
+    rshape = synth.MoEShape(256, 8, 128, 128, local_start=0, local_count=32, router="reference")
+    for bs, dist, seed in ((7, "normal", 31), (5, "skewed", 32)):
+        dref = reference.generate_input(bs, "ep8", seed, dist=dist, rank="plain", device="cpu")
+        x, scores = synth.reference_scores(rshape, bs, seed, dist)
+        assert torch.equal(u8t(x), u8t(dref["hidden_states"])), "synth.reference_scores differs"
+        save(f"router_{dist}_bs{bs}", {"E": 256, "K": 8, "mode": "renorm", "seed": seed, "dist": dist},
+             scores=scores.numpy(), topk_ids=dref["topk_ids"].numpy(), topk_weights=dref["topk_weights"].numpy())
+    g = torch.Generator().manual_seed(33)
+    logits = torch.randn((9, 128), generator=g)
+    top = torch.softmax(logits, dim=-1).topk(8, dim=-1)
+    save("router_softmax_bs9", {"E": 128, "K": 8, "mode": "softmax", "seed": 33},
+         scores=logits.numpy(), topk_ids=top.indices.to(torch.int32).numpy(),
+         topk_weights=(top.values / top.values.sum(-1, keepdim=True)).float().numpy())
     return 0
 
 

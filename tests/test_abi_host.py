@@ -80,6 +80,17 @@ def test_route_rejects_bad_arguments(lib):
     assert lib.muse_moe_route(None, 4, 8, 0, 1000, None, None, None, None) == -2
 
 
+def test_router_rejects_bad_arguments(lib):
+    f = lib.muse_moe_router_topk
+    assert f(None, 4, 256, 8, 2, None, None, None) == -1      # unknown mode
+    assert f(None, -1, 256, 8, 0, None, None, None) == -1     # negative tokens
+    assert f(None, 4, 256, 17, 0, None, None, None) == -2     # K > 16
+    assert f(None, 4, 4, 8, 0, None, None, None) == -2        # K > E
+    assert f(None, 4, 2048, 8, 0, None, None, None) == -2     # E > 1024
+    assert f(None, 0, 256, 8, 0, None, None, None) == 0       # empty batch: nothing to do
+    assert f(None, 4, 256, 8, 0, None, None, None) == -1      # null pointers
+
+
 def test_host_path_refuses_cpu_tensors(pkg):
     from muse_moe_w4a16_b200 import synth
     shape = synth.MoEShape(4, 2, 128, 128)

@@ -192,3 +192,23 @@ def test_package_byte_model_matches_oracle(pkg):
             g1 = traffic.gemm1_bytes(ids, lo, cnt, H, I)
             g2 = traffic.gemm2_bytes(ids, lo, cnt, H, I)
             assert g1 > 0 and g2 > 0
+
+
+@pytest.mark.parametrize("name", ["router_normal_bs7", "router_skewed_bs5", "router_softmax_bs9"])
+def test_router_oracle_matches_reference(name):
+    """The router restatement reproduces the reference's own routing step (generate_input's
+    topk + renormalisation) and the softmax router, on the fixtures' scores."""
+    meta, z = load(name)
+    ids, wts = orc.router_topk(z["scores"], meta["K"], meta["mode"])
+    np.testing.assert_array_equal(ids, z["topk_ids"])
+    np.testing.assert_allclose(wts, z["topk_weights"], rtol=2e-6, atol=0)
+
+
+def test_router_oracle_tie_and_nan_order():
+    scores = np.array([[1.0, 3.0, 3.0, np.nan, 2.0, 3.0],
+                       [0.5, 0.5, 0.5, 0.5, 0.5, 0.5]], dtype=np.float32)
+    ids, wts = orc.router_topk(scores, 4, "renorm")
+    np.testing.assert_array_equal(ids[0], [3, 1, 2, 5])   # NaN first, then equal 3.0s by id
+    np.testing.assert_array_equal(ids[1], [0, 1, 2, 3])
+    assert np.isnan(wts[0]).all()                           # a NaN score poisons the sum
+    np.testing.assert_allclose(wts[1], 0.25)
