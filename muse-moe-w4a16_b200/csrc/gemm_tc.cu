@@ -489,7 +489,6 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
       // track them (a commit covers the MMAs of its own thread).
       const bool leader = ptx::elect_one();
       bool ok = true;
-      const uint32_t idesc = ptx::idesc_bf16_f32(kTileM, n_box);
       const uint32_t col0 = tbase + p * kPipeCols;
       const uint32_t acc_col0 = col0 + geo.n_a * kACols;
       Ring st, ar, accr;
@@ -505,6 +504,11 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
         const int kcn = f.k_chunks, kstep = split ? kPipes : 1;
         const int kc0 = chunk_begin(p, jm, f, split);
         if (kc0 >= kcn) continue;
+        // MMA width = the item's token rows rounded up to 16, not the whole tile: a partly
+        // filled tile (the last of an expert, or an expert with few pairs) costs the tensor
+        // core only its own columns
+        const Item t = decode_item(ctl, offs, blockIdx.x + j * G, n0, n_local, n_box, mt0, mt1);
+        const uint32_t idesc = ptx::idesc_bf16_f32(kTileM, min(n_box, (t.nvalid + 15) & ~15));
         const int acc = accr.slot;
         if (!__all_sync(0xffffffffu, ptx::mbar_wait_sleep(&pc.acc_empty[acc], accr.phase ^ 1))) {
           ok = false;
