@@ -604,16 +604,27 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
 #pragma unroll
             for (int c = 0; c < 16; ++c) acc[c] += __uint_as_float(v[c]);
           }
+          // four columns at a time (independent chains the scheduler can overlap), only as many
+          // groups as the item has rows: the epilogue shares the issue slots of the dequantisers
           const int ncols = min(16, t.nvalid - cb * 16);  // warp-uniform
 #pragma unroll
-          for (int col = 0; col < 16; ++col) {
-            if (col >= ncols) break;
-            const float mine = acc[col] * gsc;
-            const float other = __shfl_xor_sync(0xffffffffu, mine, 16);
+          for (int c4 = 0; c4 < 16; c4 += 4) {
+            if (c4 >= ncols) break;
+            float act[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float mine = acc[c4 + k] * gsc;
+              const float other = __shfl_xor_sync(0xffffffffu, mine, 16);
+              act[k] = mine / (1.0f + __expf(-mine)) * other;  // lanes < 16: silu(gate) * up
+            }
             if (lane < 16) {
-              const float act = mine / (1.0f + __expf(-mine)) * other;
-              const __nv_bfloat16 hb = __float2bfloat16_rn(act);
-              a.inter[(size_t)(t.row0 + cb * 16 + col) * f.ld_out + jj] = *reinterpret_cast<const uint16_t*>(&hb);
+#pragma unroll
+              for (int k = 0; k < 4; ++k) {
+                if (c4 + k < ncols) {
+                  const __nv_bfloat16 hb = __float2bfloat16_rn(act[k]);
+                  a.inter[(size_t)(t.row0 + cb * 16 + c4 + k) * f.ld_out + jj] = *reinterpret_cast<const uint16_t*>(&hb);
+                }
+              }
             }
           }
         }
@@ -633,18 +644,31 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
 #pragma unroll
             for (int c = 0; c < 16; ++c) acc[c] += __uint_as_float(v[c]);
           }
+          const int ncols = min(16, t.nvalid - cb * 16);  // warp-uniform
 #pragma unroll
           for (int col = 0; col < 16; ++col) {
-            const int n = cb * 16 + col;
-            if (n < t.nvalid) {  // warp-uniform
-              const float y = acc[col] * wn;
-              a.ypart[(size_t)(t.row0 + n) * f.ld_out + h] = y;
-              float s2 = y * y;
+            acc[col] *= wn;
+            if (col < ncols) a.ypart[(size_t)(t.row0 + cb * 16 + col) * f.ld_out + h] = acc[col];
+            acc[col] *= acc[col];
+          }
+          // Sum of squares of each column over the warp's 32 rows, all 16 columns at once: a
+          // transposed butterfly (each round halves the columns a lane keeps, 16 shuffles in
+          // all). It adds the same pairs as a per-column xor 16/8/4/2/1 reduction, so the sums
+          // are bit-identical to it; lanes 2c and 2c + 1 end with column c.
 #pragma unroll
-              for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-              if (lane == 0) a.ssq[(size_t)(t.row0 + n) * (f.ld_out >> 5) + (h >> 5)] = s2;
+          for (int half = 8; half >= 1; half >>= 1) {
+            const bool up = lane & (2 * half);
+#pragma unroll
+            for (int i = 0; i < half; ++i) {
+              const float keep = up ? acc[half + i] : acc[i];
+              const float send = up ? acc[i] : acc[half + i];
+              acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2 * half);
             }
           }
+          acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 1);
+          const int c = (lane >> 1) & 15;
+          if (!(lane & 1) && c < ncols)
+            a.ssq[(size_t)(t.row0 + cb * 16 + c) * (f.ld_out >> 5) + (h >> 5)] = acc[0];
         }
       }
       ptx::tc_fence_before();
