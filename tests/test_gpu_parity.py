@@ -198,6 +198,34 @@ def test_layer_cfg4_large_expert_sampled_rows(pkg, synth, workload, T, rows):
     assert ok and err < 5e-3, msg
 
 
+@pytest.fixture(scope="module")
+def reference_problem_weights(synth):
+    return synth.reference_weights(synth.CONFIGS["cfg0"], device="cuda")
+
+
+@pytest.mark.parametrize("T,rows", [(1, [0]), (32, [0, 31]), (128, [0, 127]), (256, [0, 255])])
+def test_layer_reference_problem_sampled_rows(pkg, synth, reference_problem_weights, T, rows):
+    """The reference's own problem (E=256, top-8, H=I=4096, the busiest ep8 rank's 32 experts,
+    the reference's generators): every token on the GPU, sampled rows against the oracle over
+    the local experts those rows hit."""
+    shape = synth.CONFIGS["cfg0"]
+    lo, cnt = shape.local_start, shape.n_local
+    data = synth.reference_input(shape, T, seed=5000 + T)
+    ids = data["topk_ids"][rows]
+    need = sorted({int(e) for e in ids.reshape(-1).tolist() if lo <= int(e) < lo + cnt})
+    w = reference_problem_weights
+    w_np = to_numpy_weights({k: (v[need] if v.dim() > 1 or k.endswith("_gs") else v) for k, v in w.items()})
+    remap = {e: j for j, e in enumerate(need)}
+    sub = {"hidden_states": data["hidden_states"][rows],
+           "topk_ids": torch.tensor([[remap.get(int(e), -1) for e in r] for r in ids], dtype=torch.int32),
+           "topk_weights": data["topk_weights"][rows],
+           "config": dict(data["config"], local_start=0, local_count=max(len(need), 1))}
+    ref = oracle_out(sub, w_np)
+    out = pkg.moe_forward(to_device(data, DEV), w)
+    ok, msg, err, _ = orc.compare(bits(out)[rows], ref, TOL)
+    assert ok and err < 5e-3, msg
+
+
 # ----------------------------------------------------------------------------- stage checks
 
 _POS = [(6, 7, 8, 15), (22, 23, 24, 31), (2, 3, 4, 11), (18, 19, 20, 27),
