@@ -83,7 +83,7 @@ int path_of(int tokens, int top_k, int local_count) {
 }
 
 // Phases with more K chunks than this split each item over the pipelines; shorter ones give
-// each item to one pipeline.
+// each item to one pipeline (unless the kernel finds fewer than 4 items per CTA).
 constexpr int kSplitKMinChunks = 8;
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;

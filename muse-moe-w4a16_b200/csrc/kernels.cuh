@@ -46,7 +46,8 @@ struct PhaseArgs {
   const float* gs;         // [n_local] global scales
   int mode;                // 1: SiLU(gate)*up -> inter; 2: post-norm partials -> ypart, ssq
   int ld_out;              // row length of the output (I in mode 1, H in mode 2)
-  int split_k;             // split each item's chunks over the pipelines (else one pipeline per item)
+  int split_k;             // split each item's chunks over the pipelines (else one pipeline per item;
+                           // the kernel also splits any phase with fewer than 4 items per CTA)
   int b_source;            // B operand: 0 tmap_b boxes at the tile's rows (expert-grouped rows),
                            // 1 four-row gathers of x by token (tmap_x), 2 tmap_b2 boxes
   int* signal;             // per-token-tile counters: each epilogue warp adds 1 per item (or null)
