@@ -174,6 +174,18 @@ int muse_moe_peer_allreduce_bf16(const uint64_t* shares0, const uint64_t* shares
                                  muse_stream_t stream);
 
 /*
+ * The prefill-layout exchange (tokens split over the ranks, ranks x n_per_rank elements in every
+ * share): out (bf16 [n_per_rank], this rank) = sum over ranks r, in order, of elements
+ * [rank * n_per_rank, (rank + 1) * n_per_rank) of rank r's share -- this rank's tokens. Same
+ * buffers, flags, generation count and bounded waits as muse_moe_peer_allreduce_bf16 (the two
+ * calls share one generation sequence). Replaces the reduce-scatter that returns each rank the
+ * sum for its own tokens (reference.py:18-22, TASK.md:29).
+ */
+int muse_moe_peer_reduce_scatter_bf16(const uint64_t* shares0, const uint64_t* shares1,
+                                      const uint64_t* flags, int ranks, int rank, size_t n_per_rank,
+                                      void* out, muse_stream_t stream);
+
+/*
  * muse_moe_forward, with five caller-created CUDA events (cudaEvent_t, passed as void*)
  * recorded on `stream` around the kernels: [0] start, [1] before GEMM1, [2] after GEMM1,
  * [3] after GEMM2, [4] after the combine. For per-kernel timing; same results as

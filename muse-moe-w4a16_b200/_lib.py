@@ -36,6 +36,8 @@ SIGNATURES: dict[str, tuple] = {
     "muse_moe_cast_bf16": (_I, [_P, _P, ctypes.c_size_t, _P]),
     "muse_moe_peer_allreduce_bf16": (_I, [ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
                                           ctypes.POINTER(ctypes.c_uint64), _I, _I, ctypes.c_size_t, _P, _P]),
+    "muse_moe_peer_reduce_scatter_bf16": (_I, [ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
+                                               ctypes.POINTER(ctypes.c_uint64), _I, _I, ctypes.c_size_t, _P, _P]),
     "muse_moe_forward_noalloc": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I,
                                       _P, _P, _P, _P, _P, _P, _P, _P, _P]),
 }

@@ -70,7 +70,7 @@ int pick_n_box(int tokens, int top_k, int local_count) {
 
 // The single-launch (fused) path: decode batches of at most kMaxFusedPairs pairs with a small
 // token tile. Above that the separate route / gather / GEMM1 / GEMM2 / combine launches are
-// faster on B200 (measured at 256 pairs: 116 vs 120 us for E=128, H=2048, I=768).
+// faster on B200 (measured at 256 pairs, E=128, H=2048, I=768: 116.7 vs 120.8 us).
 constexpr int kMaxFusedPairs = 128;
 
 // Launch plan of a call: 2 = the whole layer in one cooperative launch, 1 = GEMM1 routes in

@@ -1,6 +1,7 @@
 // Expert-parallel exchange over NVLink peer memory: the sum of every rank's fp32 share of the
-// layer output, cast to bf16, on every rank (the all-reduce of the decode layout, done by
-// this kernel instead of a collective library).
+// layer output, cast to bf16 -- on every rank for all elements (the all-reduce of the decode
+// layout), or on each rank for its own slice of the elements (the reduce-scatter of the
+// prefill layout) -- done by this kernel instead of a collective library.
 //
 // Each rank's share lives in its own symmetric buffer; the buffers of all ranks are mapped
 // into every rank's address space (peer pointers). Every rank keeps, in its own flag array,
@@ -10,8 +11,8 @@
 //      every rank's flag array (system-scope release after a system fence, so the share's
 //      bytes -- written by the previous kernel on this stream -- are visible first);
 //   2. every block waits (acquire, bounded) until all R peer slots of its own array hold g;
-//   3. out[i] = bf16(sum over r = 0 .. R-1 of share_r[i]) from the share buffers of parity
-//      g & 1, in the same order on every rank, so all ranks produce identical bits;
+//   3. out[i] = bf16(sum over r = 0 .. R-1 of share_r[offset + i]) from the share buffers of
+//      parity g & 1, in the same order on every rank, so all ranks produce identical bits;
 //   4. the last block to finish stores g as the new counter.
 // The generation lives on the device, so a captured graph of the call stays valid across
 // replays. Callers write call g's share into buffer g & 1: a rank rewrites a buffer only two
@@ -32,6 +33,7 @@ struct PeerArgs {
   uint32_t* flags[kMaxPeers];        // flag array of rank r
   int ranks, rank;
   size_t n4;                         // elements / 4
+  size_t offset4;                    // first element / 4 (0, or this rank's slice)
   uint16_t* out;                     // bf16 [n], this rank's memory
   int* error_flag;
 };
@@ -80,7 +82,7 @@ __global__ void __launch_bounds__(256) peer_allreduce_kernel(const PeerArgs a) {
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < a.n4; i += (size_t)gridDim.x * blockDim.x) {
       float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
       for (int r = 0; r < a.ranks; ++r) {
-        const float4 v = __ldcv(reinterpret_cast<const float4*>(a.share[par][r]) + i);
+        const float4 v = __ldcv(reinterpret_cast<const float4*>(a.share[par][r]) + a.offset4 + i);
         acc.x += v.x;
         acc.y += v.y;
         acc.z += v.z;
@@ -109,12 +111,13 @@ __global__ void __launch_bounds__(256) peer_allreduce_kernel(const PeerArgs a) {
 }  // namespace
 }  // namespace muse
 
-extern "C" int muse_moe_peer_allreduce_bf16(const uint64_t* shares0, const uint64_t* shares1,
-                                            const uint64_t* flags, int ranks, int rank, size_t n,
-                                            void* out, muse_stream_t stream) {
-  using namespace muse;
+namespace muse {
+namespace {
+
+int launch_peer_sum(const uint64_t* shares0, const uint64_t* shares1, const uint64_t* flags, int ranks,
+                    int rank, size_t offset, size_t n, void* out, cudaStream_t stream) {
   if (!shares0 || !shares1 || !flags || !out || ranks < 1 || ranks > kMaxPeers || rank < 0 ||
-      rank >= ranks || n % 8)
+      rank >= ranks || n % 8 || offset % 8)
     return MUSE_ERR_INVALID_ARGUMENT;
   PeerArgs a{};
   for (int r = 0; r < ranks; ++r) {
@@ -128,10 +131,27 @@ extern "C" int muse_moe_peer_allreduce_bf16(const uint64_t* shares0, const uint6
   a.ranks = ranks;
   a.rank = rank;
   a.n4 = n / 4;
+  a.offset4 = offset / 4;
   a.out = static_cast<uint16_t*>(out);
   int rc = device_status_ptr(&a.error_flag);
   if (rc) return rc;
   const size_t blocks = (a.n4 + 255) / 256;
-  peer_allreduce_kernel<<<blocks < 296 ? (unsigned)blocks : 296u, 256, 0, (cudaStream_t)stream>>>(a);
+  peer_allreduce_kernel<<<blocks < 296 ? (unsigned)blocks : 296u, 256, 0, stream>>>(a);
   return last_launch_status();
+}
+
+}  // namespace
+}  // namespace muse
+
+extern "C" int muse_moe_peer_allreduce_bf16(const uint64_t* shares0, const uint64_t* shares1,
+                                            const uint64_t* flags, int ranks, int rank, size_t n,
+                                            void* out, muse_stream_t stream) {
+  return muse::launch_peer_sum(shares0, shares1, flags, ranks, rank, 0, n, out, (cudaStream_t)stream);
+}
+
+extern "C" int muse_moe_peer_reduce_scatter_bf16(const uint64_t* shares0, const uint64_t* shares1,
+                                                 const uint64_t* flags, int ranks, int rank,
+                                                 size_t n_per_rank, void* out, muse_stream_t stream) {
+  return muse::launch_peer_sum(shares0, shares1, flags, ranks, rank, (size_t)rank * n_per_rank, n_per_rank,
+                               out, (cudaStream_t)stream);
 }

@@ -16,8 +16,10 @@ Two layouts of the tokens:
       tensors, as in the gloo tests of the exchange logic, the shares are summed by an
       all-reduce collective instead.)
   sharded (prefill): rank r holds its own T_r tokens (T_r equal on every rank). Inputs are
-      all-gathered (x bf16, ids, weights), every rank computes its experts' share of all
-      R * T_r tokens, and a reduce-scatter returns each rank the sum for its own tokens.
+      all-gathered (x bf16, ids, weights; NCCL), every rank writes its experts' share of all
+      R * T_r tokens into its symmetric buffer, and this library's peer kernel
+      (`muse_moe_peer_reduce_scatter_bf16`) returns each rank the rank-ordered sum for its own
+      tokens over NVLink. (CPU tensors: a reduce-scatter collective, as in the gloo tests.)
 
 Collectives use fixed shapes (no counts sent to the host), so a call issues no host
 synchronisation.
@@ -159,11 +161,23 @@ class ExpertParallelMoE:
             g = torch.empty((R * t_r,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
             dist.all_gather_into_tensor(g, t, group=self.group)
             full[name] = g
-        gathered = {**data, **full}
-        part = self._local(_with_local_range(gathered, self.experts))
-        mine = torch.empty((t_r, part.shape[1]), dtype=part.dtype, device=part.device)
-        dist.reduce_scatter_tensor(mine, part, op=dist.ReduceOp.SUM, group=self.group)
-        return self._cast(mine)
+        gathered = _with_local_range({**data, **full}, self.experts)
+        if not x.is_cuda or self.state is None:
+            part = self._local(gathered)
+            mine = torch.empty((t_r, part.shape[1]), dtype=part.dtype, device=part.device)
+            dist.reduce_scatter_tensor(mine, part, op=dist.ReduceOp.SUM, group=self.group)
+            return self._cast(mine)
+        H = x.shape[1]
+        self._peer_buffers(R * t_r * H, x.device)
+        self._gen += 1
+        peer = self._peer
+        base = (self._gen & 1) * peer["cap"]
+        share = peer["buf"][base:base + R * t_r * H].view(R * t_r, H)
+        kernel_fn_partial(gathered, self.state, out=share)
+        out = torch.empty((t_r, H), dtype=torch.bfloat16, device=x.device)
+        _lib.call("muse_moe_peer_reduce_scatter_bf16", peer["shares"][0], peer["shares"][1], peer["flags"],
+                  R, self.rank, t_r * H, out.data_ptr(), torch.cuda.current_stream(x.device).cuda_stream)
+        return out
 
 
 class DecodeGraphs:

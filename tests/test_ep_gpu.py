@@ -1,6 +1,6 @@
-"""Expert parallelism on 2+ GPUs of one node: the decode exchange over NVLink peer memory and
-the prefill exchange on NCCL, every rank's output against the oracle over all experts.
-Skipped with fewer than two GPUs."""
+"""Expert parallelism on 2+ GPUs of one node: the decode exchange (all-reduce) and the prefill
+exchange (reduce-scatter, after an NCCL all-gather of the inputs) over NVLink peer memory,
+every rank's output against the oracle over all experts. Skipped with fewer than two GPUs."""
 
 from __future__ import annotations
 
@@ -67,8 +67,13 @@ def _rank_main(rank, world, port, T, result_dir):
         assert torch.equal(again.view(torch.int16), rep.view(torch.int16))
         t_r = T // world
         sl = slice(rank * t_r, (rank + 1) * t_r)
-        shard = moe.forward_sharded({**d, "hidden_states": d["hidden_states"][sl],
-                                     "topk_ids": d["topk_ids"][sl], "topk_weights": d["topk_weights"][sl]})
+        mine = {**d, "hidden_states": d["hidden_states"][sl], "topk_ids": d["topk_ids"][sl],
+                "topk_weights": d["topk_weights"][sl]}
+        shard = moe.forward_sharded(mine)
+        again = moe.forward_sharded(mine)     # the other share buffer
+        assert torch.equal(again.view(torch.int16), shard.view(torch.int16))
+        again = moe.forward_replicated(d)     # decode and prefill calls share the generation count
+        assert torch.equal(again.view(torch.int16), rep.view(torch.int16))
         torch.cuda.synchronize()
         np.save(os.path.join(result_dir, f"rep{rank}.npy"), rep.view(torch.uint16).cpu().numpy())
         np.save(os.path.join(result_dir, f"shard{rank}.npy"), shard.view(torch.uint16).cpu().numpy())
@@ -105,3 +110,5 @@ def test_expert_parallel_matches_oracle(pkg, tmp_path, T):
     got = np.concatenate([np.load(tmp_path / f"shard{r}.npy") for r in range(world)])
     ok, msg, _, _ = orc.compare(got, ref[:T_used], TOL)
     assert ok, f"sharded: {msg}"
+    if T_used == T:   # same tokens in the same order: the same shares, summed in the same order
+        np.testing.assert_array_equal(got, rep0)
