@@ -3,7 +3,7 @@
 
     python tests/golden/make_golden.py [--reference DIR]
 
-Needs the reference checkout (default /root/reference); it is only run in the build
+Needs the reference checkout (its directory via --reference or $MUSE_REFERENCE_DIR); it is only run in the build
 container, never on the GPU box, and never by the tests. The tests read the .npz files it
 writes. Every input is generated on a CPU torch.Generator, so the same bytes can be rebuilt
 by the package's synth module; the fixtures store the reference's outputs plus SHA-256
@@ -13,6 +13,7 @@ digests of inputs too large to commit.
 from __future__ import annotations
 
 import argparse
+import os
 import hashlib
 import json
 import sys
@@ -45,7 +46,7 @@ def save(name: str, meta: dict, **arrays):
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("MUSE_REFERENCE_DIR", "/root/reference"))
     a = ap.parse_args()
     sys.path.insert(0, a.reference)
     sys.path.insert(0, str(REPO))
