@@ -135,7 +135,9 @@ int launch_peer_sum(const uint64_t* shares0, const uint64_t* shares1, const uint
   a.out = static_cast<uint16_t*>(out);
   int rc = device_status_ptr(&a.error_flag);
   if (rc) return rc;
-  const size_t blocks = (a.n4 + 255) / 256;
+  // at least one block: an empty exchange (no tokens) still signals the peers and advances the
+  // generation, so every rank's count -- and the share buffer its caller writes next -- stays in step
+  const size_t blocks = a.n4 == 0 ? 1 : (a.n4 + 255) / 256;
   peer_allreduce_kernel<<<blocks < 296 ? (unsigned)blocks : 296u, 256, 0, stream>>>(a);
   return last_launch_status();
 }

@@ -91,6 +91,9 @@ class ExpertParallelMoE:
         """Decode layout: the same T tokens on every rank -> bf16 [T, H] on every rank."""
         x = data["hidden_states"]
         local = _with_local_range(data, self.experts)
+        if x.shape[0] == 0:
+            # every rank has the same (empty) batch: nothing to exchange, generation unchanged
+            return torch.empty((0, x.shape[1]), dtype=torch.bfloat16, device=x.device)
         if not x.is_cuda or self.state is None:
             part = self._local(local)
             dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
@@ -154,6 +157,8 @@ class ExpertParallelMoE:
         x, ids, wts = data["hidden_states"], data["topk_ids"], data["topk_weights"]
         t_r = x.shape[0]
         R = self.world
+        if t_r == 0:   # T_r is the same on every rank: no rank exchanges anything
+            return torch.empty((0, x.shape[1]), dtype=torch.bfloat16, device=x.device)
         full = {}
         for name, t in (("hidden_states", x), ("topk_ids", ids.to(torch.int32)),
                         ("topk_weights", wts.to(torch.float32))):

@@ -81,6 +81,11 @@ def _rank_main(rank, world, port, layout, T, result_dir):
         shape, w, d, wn = _problem(11, T)
         moe = ep.ExpertParallelMoE(w, n_experts=shape.n_experts, local_fn=_oracle_partial(wn, shape.inter),
                                    cast_fn=_oracle_cast)
+        empty = {**d, "hidden_states": d["hidden_states"][:0], "topk_ids": d["topk_ids"][:0],
+                 "topk_weights": d["topk_weights"][:0]}
+        call = moe.forward_replicated if layout == "replicated" else moe.forward_sharded
+        none = call(empty)   # an empty batch on every rank: empty result, no exchange
+        assert none.shape == (0, d["hidden_states"].shape[1]) and none.dtype == torch.bfloat16
         if layout == "replicated":
             out = moe.forward_replicated(d)
         else:
