@@ -47,6 +47,9 @@ def e4m3_table() -> np.ndarray:
 
 _E2M1 = e2m1_table()
 _E4M3 = e4m3_table()
+# float32 [256, 2]: the two values of a packed code byte (low nibble first, nvfp4.py:5-6), so a
+# packed row is unpacked by one table lookup per byte
+_E2M1_PAIR = np.stack([_E2M1[np.arange(256) & 0x0F], _E2M1[np.arange(256) >> 4]], axis=1)
 
 
 def bf16_to_f32(bits: np.ndarray) -> np.ndarray:
@@ -67,10 +70,7 @@ def f32_to_bf16(x: np.ndarray) -> np.ndarray:
 def unpack_e2m1(packed: np.ndarray) -> np.ndarray:
     """uint8 [..., K/2] -> float32 [..., K]; element 2i is the low nibble (nvfp4.py:40-47)."""
     p = np.asarray(packed, dtype=np.uint8)
-    out = np.empty(p.shape[:-1] + (p.shape[-1] * 2,), dtype=np.float32)
-    out[..., 0::2] = _E2M1[p & 0x0F]
-    out[..., 1::2] = _E2M1[p >> 4]
-    return out
+    return np.take(_E2M1_PAIR, p, axis=0).reshape(p.shape[:-1] + (p.shape[-1] * 2,))
 
 
 def dequantize(packed: np.ndarray, sf: np.ndarray, gs: float | np.floating) -> np.ndarray:
@@ -171,7 +171,7 @@ def ref_kernel(x_bits, topk_ids, topk_weights, weights: dict, local_start: int, 
         w2 = dequantize(weights["w2"][e], weights["w2_sf"][e], weights["w2_gs"][e])
         y = inter @ w2.T
         contrib = post_expert_norm(y, weights["post_norm_w"]) * wts[tok, slot][:, None]
-        np.add.at(out, tok, contrib)
+        _add_rows(out, tok, contrib)
     if return_f32:
         return out
     return f32_to_bf16(out)
@@ -203,8 +203,18 @@ def ref_kernel_threads(x_bits, topk_ids, topk_weights, weights: dict, local_star
     out = np.zeros(x.shape, dtype=np.float32)
     with ThreadPoolExecutor(max_workers=max(1, threads)) as ex:
         for tok, contrib in ex.map(one, experts):
-            np.add.at(out, tok, contrib)
+            _add_rows(out, tok, contrib)
     return f32_to_bf16(out)
+
+
+def _add_rows(out: np.ndarray, tok: np.ndarray, contrib: np.ndarray) -> None:
+    """out[tok[i]] += contrib[i] in fp32, as index_add_ does (reference.py:106). A token meets an
+    expert at most once when its top-k ids are distinct, and then one indexed add is the same
+    arithmetic as np.add.at; repeated ids fall back to it."""
+    if tok.size and np.unique(tok).size == tok.size:
+        out[tok] += contrib
+    else:
+        np.add.at(out, tok, contrib)
 
 
 def compare(out_bits: np.ndarray, ref_bits: np.ndarray, tol: float = REL_L2_TOL):

@@ -46,8 +46,12 @@ def save(name: str, meta: dict, **arrays):
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("MUSE_REFERENCE_DIR", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("MUSE_REFERENCE_DIR"),
+                    help="directory holding the reference's reference.py / nvfp4.py / checks.py "
+                         "(or set MUSE_REFERENCE_DIR)")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("give --reference DIR or set MUSE_REFERENCE_DIR")
     sys.path.insert(0, a.reference)
     sys.path.insert(0, str(REPO))
     import checks  # noqa: F401  (reference)

@@ -117,7 +117,7 @@ def test_layer_cfg2_decode(pkg, synth, cfg2_weights, T):
     assert err < 5e-3
 
 
-@pytest.mark.parametrize("T", [128, 257])
+@pytest.mark.parametrize("T", [128, 256, 257, 512])
 def test_layer_cfg3_zipf(pkg, synth, cfg2_weights, T):
     _, w = cfg2_weights
     shape = synth.CONFIGS["cfg3"]
@@ -172,58 +172,6 @@ def test_layer_cuda_graph_replay(pkg, synth, cfg2_weights):
         torch.cuda.synchronize()
         ok, msg, *_ = orc.compare(bits(out), oracle_out(d, w_np), TOL)
         assert ok, msg
-
-
-@pytest.mark.parametrize("workload,T,rows", [("cfg4", 32, [0, 13, 31]), ("cfg4", 256, [0, 100, 255]),
-                                             ("cfg5", 4096, [0, 1777, 4095])])
-def test_layer_cfg4_large_expert_sampled_rows(pkg, synth, workload, T, rows):
-    """E=256, H=7168, I=2048 at decode (T=32, 256: one and three launches) and prefill (T=4096,
-    Zipf router, 128-token tiles, five launches): every token is computed on the GPU, 3 rows are
-    checked against the oracle (the oracle dequantises only their experts)."""
-    shape = synth.CONFIGS[workload]
-    data = synth.baseline_input(shape, T, seed=4000 + T)
-    need = sorted(set(data["topk_ids"][rows].reshape(-1).tolist()))
-    w = synth.baseline_weights(shape, seed=5252, device="cuda")
-    w_np = to_numpy_weights({k: (v[need] if v.dim() > 1 or k.endswith("_gs") else v) for k, v in w.items()})
-    # oracle over the needed experts only: remap their ids to 0..len(need)-1
-    remap = {e: j for j, e in enumerate(need)}
-    sub = {"hidden_states": data["hidden_states"][rows],
-           "topk_ids": torch.tensor([[remap.get(int(e), -1) for e in r] for r in data["topk_ids"][rows]],
-                                    dtype=torch.int32),
-           "topk_weights": data["topk_weights"][rows],
-           "config": dict(data["config"], local_start=0, local_count=len(need))}
-    ref = oracle_out(sub, w_np)
-    out = pkg.moe_forward(to_device(data, DEV), w)
-    ok, msg, err, _ = orc.compare(bits(out)[rows], ref, TOL)
-    assert ok and err < 5e-3, msg
-
-
-@pytest.fixture(scope="module")
-def reference_problem_weights(synth):
-    return synth.reference_weights(synth.CONFIGS["cfg0"], device="cuda")
-
-
-@pytest.mark.parametrize("T,rows", [(1, [0]), (32, [0, 31]), (128, [0, 127]), (256, [0, 255])])
-def test_layer_reference_problem_sampled_rows(pkg, synth, reference_problem_weights, T, rows):
-    """The reference's own problem (E=256, top-8, H=I=4096, the busiest ep8 rank's 32 experts,
-    the reference's generators): every token on the GPU, sampled rows against the oracle over
-    the local experts those rows hit."""
-    shape = synth.CONFIGS["cfg0"]
-    lo, cnt = shape.local_start, shape.n_local
-    data = synth.reference_input(shape, T, seed=5000 + T)
-    ids = data["topk_ids"][rows]
-    need = sorted({int(e) for e in ids.reshape(-1).tolist() if lo <= int(e) < lo + cnt})
-    w = reference_problem_weights
-    w_np = to_numpy_weights({k: (v[need] if v.dim() > 1 or k.endswith("_gs") else v) for k, v in w.items()})
-    remap = {e: j for j, e in enumerate(need)}
-    sub = {"hidden_states": data["hidden_states"][rows],
-           "topk_ids": torch.tensor([[remap.get(int(e), -1) for e in r] for r in ids], dtype=torch.int32),
-           "topk_weights": data["topk_weights"][rows],
-           "config": dict(data["config"], local_start=0, local_count=max(len(need), 1))}
-    ref = oracle_out(sub, w_np)
-    out = pkg.moe_forward(to_device(data, DEV), w)
-    ok, msg, err, _ = orc.compare(bits(out)[rows], ref, TOL)
-    assert ok and err < 5e-3, msg
 
 
 # ----------------------------------------------------------------------------- stage checks
