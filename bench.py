@@ -1,23 +1,28 @@
 """Benchmark of the routed W4A16 MoE layer on B200 (one JSON line on stdout, rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl muse|reference]
-                    [--workload cfg2] [--tokens 1,4,16,32]
+                    [--workload cfg4] [--tokens 1,32,256] [--no-cpu-baseline] [--no-secondary]
 
 Metric: MoE layer us/call and achieved HBM GB/s (% of the measured B200 copy
-bandwidth) per token count. Default workload: configuration 2 (decode; E=128, top-8, H=2048,
-I=768; T in {1, 4, 16, 32}; uniform router; NVFP4 weights from N(0, 0.02)).
+bandwidth) per token count. Default workload: configuration 4 -- large-expert decode (E=256,
+top-8, H=7168, I=2048, uniform router, NVFP4 weights from N(0, 0.02); T in {1, 32, 256}), the
+configuration BASELINE.json runs on one B200 and then expert-parallel over 2/4/8 GPUs. On one
+GPU the line also carries configuration 2 (E=128, H=2048, I=768, T in {1, 4, 16, 32}, the
+small-expert decode sweep) as a secondary device-timed block.
 
-A step is one layer call at every token count of the sweep. Each call is a CUDA-graph
-replay of kernel_fn, preceded (outside its timing) by a 512 MiB write that flushes the L2,
-and timed with CUDA events on the launching stream. `value` is the geometric mean over the
-sweep of the mean us/call; `per_T` lists each token count. Under torchrun (N > 1) the layer
-runs expert-parallel: each rank holds E/N experts, every rank sees all tokens (the decode
-layout), the fp32 shares are summed over NVLink peer memory by the library's own kernel inside
-the captured graphs, and times are the max over ranks (strong scaling: the same call, split N
-ways).
+A step is one layer call at every token count of the sweep. Each call is a CUDA-graph replay,
+preceded (outside its timing) by a 512 MiB write that flushes the L2, and timed with CUDA events
+on the launching stream. `value` is the geometric mean over the sweep of the mean us/call;
+`per_T` lists each token count. Under torchrun (N > 1) the layer runs expert-parallel: rank r
+holds its contiguous block of E/N experts, every rank sees all tokens (the decode layout), the
+fp32 shares are summed over NVLink peer memory by the library's own kernel inside the captured
+graphs, and times are the max over ranks -- the same call split N ways (strong scaling). Before
+timing, every line checks its outputs: on one GPU against the CPU oracle, on N GPUs the
+expert-parallel output against the single-GPU layer (itself pinned to the oracle) and every
+rank's bits against rank 0's; the process exits non-zero if a check fails.
 
-`--impl reference` times the CPU oracle (the reference's fp32 dequantise-then-accumulate
-path restated in numpy, all host cores) on the same workload; rank 0 only.
+`--impl reference` times the CPU oracle (the reference's fp32 dequantise-then-accumulate path
+restated in numpy, all host cores) on the same workload; rank 0 only.
 """
 
 from __future__ import annotations
@@ -44,6 +49,12 @@ import __graft_entry__  # noqa: E402
 FLUSH_BYTES = 512 << 20
 PEAKS_FILE = REPO / "MEASURED_PEAKS.json"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+DEFAULT_WORKLOAD = "cfg4"
+SECONDARY_WORKLOAD = "cfg2"
+PARITY_TOL = 1.5e-2          # checks.compare's tolerance (reference.py:25)
+# ncu per-launch DRAM traffic of the dominant kernel, recorded from the capture summarised in
+# profiles/ (read here so the line can carry it next to the algorithmic bytes)
+TRAFFIC_FILE = REPO / "profiles" / "traffic.json"
 
 
 def parse_args(argv=None):
@@ -52,9 +63,10 @@ def parse_args(argv=None):
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("muse", "reference"), default="muse")
-    ap.add_argument("--workload", default="cfg2")
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
     ap.add_argument("--tokens", default=None, help="comma list overriding the workload's sweep")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-secondary", action="store_true", help="skip the secondary cfg2 block")
     return ap.parse_args(argv)
 
 
@@ -97,6 +109,16 @@ def max_over_ranks(world, values: list[float]) -> list[float]:
     t = torch.tensor(values, dtype=torch.float64, device="cuda")
     torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
     return t.tolist()
+
+
+def gather_ranks(world, values: list[float]) -> list[list[float]]:
+    """Every rank's list (same length on every rank), rank order."""
+    if world == 1:
+        return [values]
+    t = torch.tensor(values, dtype=torch.float64, device="cuda")
+    out = [torch.empty_like(t) for _ in range(world)]
+    torch.distributed.all_gather(out, t)
+    return [o.tolist() for o in out]
 
 
 # ----------------------------------------------------------------------------- clocks
@@ -159,9 +181,9 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------- workloads
 
-def workload(args, pkg_synth):
-    shape = pkg_synth.CONFIGS[args.workload]
-    tokens = tuple(int(t) for t in args.tokens.split(",")) if args.tokens else pkg_synth.TOKENS[args.workload]
+def sweep(synth, name: str, tokens_arg: str | None):
+    shape = synth.CONFIGS[name]
+    tokens = tuple(int(t) for t in tokens_arg.split(",")) if tokens_arg else synth.TOKENS[name]
     return shape, tokens
 
 
@@ -188,69 +210,25 @@ def make_input(synth, shape, workload_name: str, t: int):
     return synth.baseline_input(shape, t, seed=input_seed(workload_name, t))
 
 
-def published_ratio(args, tokens, value):
+def published_ratio(name, tokens, value):
     """value / the published geomean over the same token counts, when the workload has one."""
-    pub = PUBLISHED_US.get(args.workload)
+    pub = PUBLISHED_US.get(name)
     if not pub or any(t not in pub for t in tokens):
         return None
     return round(value / geomean([pub[t] for t in tokens]), 4)
 
 
-# ----------------------------------------------------------------------------- reference arm
-
-def run_reference(args, world, rank):
-    if rank != 0:
-        return 0
-    from oracle import moe_oracle as orc
-
-    pkg = __graft_entry__.load_package()
-    from muse_moe_w4a16_b200 import synth
-    shape, tokens = workload(args, synth)
-    cores = os.cpu_count() or 1
-    w = make_weights(synth, shape, "cuda" if torch.cuda.is_available() else "cpu")
-    w_np = {k: (v.view(torch.uint8) if v.dtype == torch.float8_e4m3fn else
+def numpy_weights(w):
+    return {k: (v.view(torch.uint8) if v.dtype == torch.float8_e4m3fn else
                 v.view(torch.uint16) if v.dtype == torch.bfloat16 else v).cpu().numpy() for k, v in w.items()}
-    del pkg
-    inputs = {t: make_input(synth, shape, args.workload, t) for t in tokens}
-
-    def call(t):
-        d = inputs[t]
-        orc.ref_kernel_threads(d["hidden_states"].view(torch.uint16).numpy(), d["topk_ids"].numpy(),
-                               d["topk_weights"].numpy(), w_np, shape.local_start, shape.n_local,
-                               shape.inter, threads=cores)
-
-    for i in range(args.warmup):
-        call(tokens[0])
-    samples = {t: [] for t in tokens}
-    n = max(args.steps, len(tokens))
-    for i in range(n):
-        t = tokens[i % len(tokens)]
-        t0 = time.perf_counter()
-        call(t)
-        samples[t].append((time.perf_counter() - t0) * 1e6)
-    per_t = {t: statistics.mean(v) for t, v in samples.items()}
-    value = geomean(list(per_t.values()))
-    line = {
-        "impl": "reference", "metric": metric_name(args), "value": value, "unit": "us/call",
-        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
-        "ms_per_step": sum(per_t.values()) / 1e3, "higher_is_better": False, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": config_block(args, shape, tokens),
-        "per_T": [{"T": t, "us": per_t[t], "samples": len(samples[t])} for t in tokens],
-        "cpu_baseline": {"value": value, "unit": "us/call", "cores": cores, "kind": "port",
-                         "sample": f"one layer call per step, token counts {list(tokens)} in rotation"},
-        "e2e": {"value": value, "unit": "us/call", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
-    }
-    print(json.dumps(line), flush=True)
-    return 0
 
 
-def metric_name(args):
-    return f"MoE layer us/call (geomean over the token sweep), {args.workload}"
+def metric_name(name):
+    return f"MoE layer us/call (geomean over the token sweep), {name}"
 
 
-def config_block(args, shape, tokens):
-    return {"workload": f"{args.workload}: E={shape.n_experts} top-{shape.top_k} H={shape.hidden} "
+def config_block(name, shape, tokens, n_gpus):
+    return {"workload": f"{name}: E={shape.n_experts} top-{shape.top_k} H={shape.hidden} "
                         f"I={shape.inter} local=[{shape.local_start},{shape.local_start + shape.n_local}) "
                         f"router={shape.router} T={list(tokens)}",
             "weights": ("NVFP4 from the reference's generators (log-normal e4m3 block scales, "
@@ -258,28 +236,97 @@ def config_block(args, shape, tokens):
                         if shape.router.startswith("reference") else
                         "NVFP4 (e2m1, e4m3 block-16 scales, fp32 global scale) from N(0,0.02)"),
             "activations": "bf16 N(0,1)", "l2": "flushed by a 512 MiB write before every timed call",
-            "parallelism": (f"ep{args.gpus}: experts split in contiguous blocks, tokens replicated, "
-                            "fp32 shares summed over NVLink peer memory") if args.gpus > 1 else "single GPU"}
+            "parallelism": (f"ep{n_gpus}: experts split in contiguous blocks, tokens replicated, "
+                            "fp32 shares summed over NVLink peer memory") if n_gpus > 1 else "single GPU"}
+
+
+# ----------------------------------------------------------------------------- reference arm
+
+def run_reference(args, world, rank):
+    """The CPU oracle on the same workload, all host cores. Each step is one sweep over the token
+    counts; at each count the oracle runs over a bounded sample of the local experts the batch
+    hits (at most as many experts as host threads, the lowest ids; the batch's pairs with other
+    experts are left out) and its time is scaled by (experts hit) / (experts sampled): the
+    oracle's cost is per expert (fp32 dequantisation of its weights dominates), so the scaled
+    time estimates the whole call. The whole run ends in about a minute."""
+    if rank != 0:
+        return 0
+    from oracle import moe_oracle as orc
+
+    pkg = __graft_entry__.load_package()
+    from muse_moe_w4a16_b200 import synth
+    shape, tokens = sweep(synth, args.workload, args.tokens)
+    cores = os.cpu_count() or 1
+    w_np = numpy_weights(make_weights(synth, shape, "cuda" if torch.cuda.is_available() else "cpu"))
+    del pkg
+    inputs = {t: make_input(synth, shape, args.workload, t) for t in tokens}
+    lo, cnt = shape.local_start, shape.n_local
+    samples = {}
+    for t in tokens:
+        ids = inputs[t]["topk_ids"].numpy()
+        hit = sorted({int(e) for e in ids.reshape(-1) if lo <= e < lo + cnt})
+        keep = hit[:cores]
+        masked = np.where(np.isin(ids, keep), ids, -1).astype(np.int32)
+        samples[t] = (masked, len(hit) / max(len(keep), 1), len(keep), len(hit))
+
+    def call(t):
+        d = inputs[t]
+        masked = samples[t][0]
+        orc.ref_kernel_threads(d["hidden_states"].view(torch.uint16).numpy(), masked,
+                               d["topk_weights"].numpy(), w_np, lo, cnt, shape.inter, threads=cores)
+
+    for _ in range(args.warmup):
+        for t in tokens:
+            call(t)
+    per_step, per_t_samples = [], {t: [] for t in tokens}
+    for _ in range(args.steps):
+        step_us = 0.0
+        for t in tokens:
+            t0 = time.perf_counter()
+            call(t)
+            us = (time.perf_counter() - t0) * 1e6 * samples[t][1]
+            per_t_samples[t].append(us)
+            step_us += us
+        per_step.append(step_us)
+    per_t = {t: statistics.mean(v) for t, v in per_t_samples.items()}
+    value = geomean(list(per_t.values()))
+    sample_txt = ("each step: one oracle call per token count over a sample of the experts hit "
+                  + ", ".join(f"T={t}: {samples[t][2]} of {samples[t][3]}" for t in tokens)
+                  + f" ({cores} threads), times scaled by experts hit / experts sampled")
+    line = {
+        "impl": "reference", "metric": metric_name(args.workload), "value": value, "unit": "us/call",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": statistics.mean(per_step) / 1e3, "higher_is_better": False, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": config_block(args.workload, shape, tokens, args.gpus),
+        "per_T": [{"T": t, "us": per_t[t], "experts_sampled": samples[t][2], "experts_hit": samples[t][3]}
+                  for t in tokens],
+        "cpu_baseline": {"value": value, "unit": "us/call", "cores": cores, "kind": "port",
+                         "sample": sample_txt},
+        "e2e": {"value": value, "unit": "us/call", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
 
 
 # ----------------------------------------------------------------------------- CPU baseline leg
 
-def cpu_baseline(shape, tokens, w, inputs):
+def cpu_baseline(shape, tokens, w_np, inputs):
+    """The oracle over the whole sweep (all host threads); also returns its outputs, which the
+    single-GPU line's parity check compares against."""
     from oracle import moe_oracle as orc
     cores = os.cpu_count() or 1
-    w_np = {k: (v.view(torch.uint8) if v.dtype == torch.float8_e4m3fn else
-                v.view(torch.uint16) if v.dtype == torch.bfloat16 else v).cpu().numpy() for k, v in w.items()}
-    per_t = {}
+    per_t, outs = {}, {}
     for t in tokens:
         d = inputs[t]
         t0 = time.perf_counter()
-        orc.ref_kernel_threads(d["hidden_states"].cpu().view(torch.uint16).numpy(), d["topk_ids"].cpu().numpy(),
-                               d["topk_weights"].cpu().numpy(), w_np, shape.local_start, shape.n_local,
-                               shape.inter, threads=cores)
+        outs[t] = orc.ref_kernel_threads(d["hidden_states"].cpu().view(torch.uint16).numpy(),
+                                         d["topk_ids"].cpu().numpy(), d["topk_weights"].cpu().numpy(), w_np,
+                                         shape.local_start, shape.n_local, shape.inter, threads=cores)
         per_t[t] = (time.perf_counter() - t0) * 1e6
     return {"value": geomean(list(per_t.values())), "unit": "us/call", "cores": cores, "kind": "port",
             "sample": f"one call per token count {list(tokens)} (numpy oracle, {cores} threads)",
-            "per_T_us": {str(t): v for t, v in per_t.items()}}
+            "per_T_us": {str(t): v for t, v in per_t.items()}}, outs
 
 
 # ----------------------------------------------------------------------------- our arm
@@ -294,198 +341,330 @@ class _Eager:
         self.fn()
 
 
-def run_muse(args, world, rank, local):
-    pkg = __graft_entry__.load_package()
-    from muse_moe_w4a16_b200 import _lib, synth, traffic
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.uint16).numpy()
 
-    dev = torch.device("cuda", local)
-    shape, tokens = workload(args, synth)
-    w = make_weights(synth, shape, dev)
-    if world > 1:
-        # expert-parallel: this rank repacks and computes only its block of experts; every
-        # rank holds all tokens (decode layout) and the fp32 shares are all-reduced over NCCL
-        from muse_moe_w4a16_b200 import ep
-        moe = ep.ExpertParallelMoE(w)
-        moe.reserve_decode(max(tokens), shape.hidden, dev)   # before any graph is captured
-        layer_call = moe.forward_replicated
-        experts = moe.experts
-    else:
-        state = pkg.prepare(w)
-        layer_call = lambda d: pkg.kernel_fn(d, state)  # noqa: E731
-        experts = range(shape.local_start, shape.local_start + shape.n_local)
-    inputs = {t: make_input(synth, shape, args.workload, t) for t in tokens}
-    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
-    stream = torch.cuda.current_stream(dev)
 
-    # Device-resident inputs and one captured graph per token count (with N > 1 a pair of
-    # graphs, one per exchange-buffer parity: the decode call holds no collective library call).
-    graphs, outs, dev_in = {}, {}, {}
-    for t in tokens:
-        d = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in inputs[t].items()}
-        dev_in[t] = d
-        outs[t] = layer_call(d)          # eager first call (kernel attributes, communicator)
-        torch.cuda.synchronize()
-        if world == 1:
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                outs[t] = layer_call(d)
-        else:
-            g = moe.decode_graphs(d)
-        graphs[t] = g
+class Bench:
+    def __init__(self, args, world, rank, local):
+        self.args, self.world, self.rank, self.local = args, world, rank, local
+        self.pkg = __graft_entry__.load_package()
+        from muse_moe_w4a16_b200 import _lib, synth, traffic
+        self._lib, self.synth, self.traffic = _lib, synth, traffic
+        self.dev = torch.device("cuda", local)
+        self.flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=self.dev)
+        self.stream = torch.cuda.current_stream(self.dev)
 
-    # End-to-end: pinned host inputs -> device, layer call, result -> pinned host. One graph
-    # per token count, built, timed and released in turn (see e2e_time below).
-    h2d = sum(inputs[t][k].numel() * inputs[t][k].element_size()
-              for t in tokens for k in ("hidden_states", "topk_ids", "topk_weights"))
-    d2h = sum(t * shape.hidden * 2 for t in tokens)
-
-    def e2e_graph(t):
-        hi = {k: (v.pin_memory() if isinstance(v, torch.Tensor) else v) for k, v in inputs[t].items()}
-        ho = torch.empty((t, shape.hidden), dtype=torch.bfloat16).pin_memory()
-        d = {k: (torch.empty_like(v, device=dev) if isinstance(v, torch.Tensor) else v) for k, v in hi.items()}
-        for k in ("hidden_states", "topk_ids", "topk_weights"):
-            d[k].copy_(hi[k], non_blocking=True)
-        layer_call(d)
-        torch.cuda.synchronize()
-
-        def e2e_step():
-            for k in ("hidden_states", "topk_ids", "topk_weights"):
-                d[k].copy_(hi[k], non_blocking=True)
-            ho.copy_(layer_call(d), non_blocking=True)
-
-        if world == 1:
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g):
-                e2e_step()
-        else:
-            g = _Eager(e2e_step)
-        return g, (hi, ho, d)
-
-    def timed(graph_map, steps, read_flush=False):
+    def timed(self, graph_map, tokens, steps, read_flush=False):
+        flush_words = self.flush.view(torch.int64)
+        sink = torch.zeros((), dtype=torch.int64, device=self.dev)
         ev = {t: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                   for _ in range(steps)] for t in tokens}
         for i in range(steps):
             for t in tokens:
                 if read_flush:
-                    flush_sink.copy_(flush_words.amax())
+                    sink.copy_(flush_words.amax())
                 else:
-                    flush.zero_()
-                ev[t][i][0].record(stream)
+                    self.flush.zero_()
+                ev[t][i][0].record(self.stream)
                 graph_map[t].replay()
-                ev[t][i][1].record(stream)
+                ev[t][i][1].record(self.stream)
         return ev
 
-    flush_words = flush.view(torch.int64)
-    flush_sink = torch.zeros((), dtype=torch.int64, device=dev)
+    def measure(self, name, tokens, full):
+        """Time one workload. `full`: also the end-to-end pass, the reference-harness-style
+        pass, the CPU baseline and the parity check (the headline workload)."""
+        args, world, dev, synth, traffic, _lib, pkg = (self.args, self.world, self.dev, self.synth,
+                                                      self.traffic, self._lib, self.pkg)
+        shape = synth.CONFIGS[name]
+        w = make_weights(synth, shape, dev)
+        moe = None
+        if world > 1:
+            # expert-parallel: this rank repacks and computes only its block of experts; every
+            # rank holds all tokens (decode layout); the exchange runs over NVLink peer memory
+            from muse_moe_w4a16_b200 import ep
+            moe = ep.ExpertParallelMoE(w)
+            moe.reserve_decode(max(tokens), shape.hidden, dev)   # before any graph is captured
+            layer_call = moe.forward_replicated
+            n_local = len(moe.experts)
+        else:
+            state = pkg.prepare(w)
+            layer_call = lambda d: pkg.kernel_fn(d, state)  # noqa: E731
+            n_local = shape.n_local
+        inputs = {t: make_input(synth, shape, name, t) for t in tokens}
 
-    # warm-up (untimed)
-    timed(graphs, args.warmup)
-    torch.cuda.synchronize()
+        graphs, outs, dev_in = {}, {}, {}
+        for t in tokens:
+            d = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in inputs[t].items()}
+            dev_in[t] = d
+            outs[t] = layer_call(d)          # eager first call (kernel attributes, exchange buffers)
+            torch.cuda.synchronize()
+            if world == 1:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    outs[t] = layer_call(d)
+            else:
+                g = moe.decode_graphs(d)
+            graphs[t] = g
 
-    with ClockSampler(local) as clocks:
-        barrier(world)
-        torch.cuda.synchronize()
-        ev = timed(graphs, args.steps)
-        torch.cuda.synchronize()
-        barrier(world)
-    # One end-to-end graph alive at a time: a process holding the layer graphs plus every
-    # token count's end-to-end graph at once (cfg3: T = 128, 256, 512) crashed inside the graph
-    # launch on this pool, while any subset ran clean.
-    per_t_e2e = []
-    for t in tokens:
-        g, keep = e2e_graph(t)
-        evs = []
-        for i in range(max(1, args.warmup) + args.steps):
-            flush.zero_()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            g.replay()
-            e1.record(stream)
-            if i >= max(1, args.warmup):
-                evs.append((e0, e1))
-        torch.cuda.synchronize()
-        per_t_e2e.append(statistics.mean(a.elapsed_time(b) * 1e3 for a, b in evs))
-        del g, keep
+        parity = self.parity_ep(shape, w, tokens, dev_in, graphs) if (full and world > 1) else None
+        w_np = numpy_weights(w) if (full and world == 1 and not args.no_cpu_baseline) else None
+        del w
 
-    # The reference harness's way (TASK.md:66-70), single GPU only: L2 emptied by *reading* a
-    # buffer larger than L2 (clean lines; the headline's write leaves dirty ones that the call
-    # must write back), and the fixed cost of a graph replay, which that harness subtracts.
-    ref_style = {}
-    if world == 1:
+        self.timed(graphs, tokens, args.warmup)
+        torch.cuda.synchronize()
+        clocks = None
+        if full:
+            with ClockSampler(self.local) as sampler:
+                barrier(world)
+                torch.cuda.synchronize()
+                ev = self.timed(graphs, tokens, args.steps)
+                torch.cuda.synchronize()
+                barrier(world)
+            clocks = sampler.summary()
+        else:
+            barrier(world)
+            ev = self.timed(graphs, tokens, args.steps)
+            torch.cuda.synchronize()
+        per_t = max_over_ranks(world, [statistics.mean(a.elapsed_time(b) * 1e3 for a, b in ev[t]) for t in tokens])
+        gpu_out = None
+        if full and world == 1:   # the outputs the parity check compares (one more replay each)
+            gpu_out = {}
+            for t in tokens:
+                graphs[t].replay()
+                torch.cuda.synchronize()
+                gpu_out[t] = bits(outs[t])
+
+        res = {"name": name, "shape": shape, "tokens": tokens, "per_t": per_t, "inputs": inputs,
+               "n_local": n_local, "clocks": clocks, "parity": parity}
+        if full:
+            res["e2e"] = self.e2e(inputs, shape, tokens, layer_call)
+        if full and world == 1:
+            res["ref_style"] = self.reference_style(graphs, tokens)
+        if world == 1:
+            res["stage_us"] = self.stages(tokens, dev_in, state, outs)
+        elif full:
+            res["rank_split"] = self.rank_split(tokens, dev_in, moe)
+        del graphs
+        torch.cuda.synchronize()
+        if w_np is not None:
+            cpu, ref_outs = cpu_baseline(shape, tokens, w_np, inputs)
+            res["cpu_baseline"] = cpu
+            res["parity"] = self.parity_oracle(tokens, gpu_out, ref_outs)
+        return res
+
+    # -- checks -----------------------------------------------------------------------------
+
+    def parity_oracle(self, tokens, gpu_out, ref_outs):
+        from oracle import moe_oracle as orc
+        rows = {}
+        for t in tokens:
+            ok, _, err, worst = orc.compare(gpu_out[t], ref_outs[t], PARITY_TOL)
+            rows[str(t)] = {"rel_l2": float(err), "worst_row": float(worst), "ok": bool(ok)}
+        return {"against": "CPU oracle (numpy restatement of reference.py:93-107), every row",
+                "tol": PARITY_TOL, "per_T": rows, "ok": all(r["ok"] for r in rows.values())}
+
+    def parity_ep(self, shape, w, tokens, dev_in, graphs):
+        """Expert-parallel output (a graph replay) against the single-GPU layer on rank 0, and
+        every rank's bits against rank 0's."""
+        from oracle import moe_oracle as orc
+        world, rank, pkg = self.world, self.rank, self.pkg
+        state = pkg.prepare(w) if rank == 0 else None
+        rows = {}
+        all_ok = True
+        for t in tokens:
+            got = graphs[t].replay()
+            torch.cuda.synchronize()
+            mine = got.view(torch.int16).clone()
+            ref0 = mine.clone()
+            torch.distributed.broadcast(ref0, 0)
+            equal = torch.tensor([1 if torch.equal(mine, ref0) else 0], device=self.dev)
+            torch.distributed.all_reduce(equal, op=torch.distributed.ReduceOp.MIN)
+            row = {"ranks_bit_equal": bool(equal.item())}
+            if rank == 0:
+                single = pkg.kernel_fn(dev_in[t], state)
+                torch.cuda.synchronize()
+                ok, _, err, worst = orc.compare(bits(got), bits(single), PARITY_TOL)
+                row.update({"rel_l2": float(err), "worst_row": float(worst), "ok": bool(ok)})
+                all_ok &= ok and row["ranks_bit_equal"]
+            rows[str(t)] = row
+        del state
+        torch.cuda.empty_cache()
+        flag = torch.tensor([1 if all_ok else 0], device=self.dev)
+        torch.distributed.broadcast(flag, 0)
+        self._lib.device_status(reset=True)
+        return {"against": "single-GPU layer on rank 0 (pinned to the CPU oracle by the tests); "
+                           "every rank's bits against rank 0's",
+                "tol": PARITY_TOL, "per_T": rows, "ok": bool(flag.item())}
+
+    # -- extra passes -----------------------------------------------------------------------
+
+    def e2e(self, inputs, shape, tokens, layer_call):
+        """Pinned host inputs -> device, layer call, result -> pinned host, timed per call. One
+        end-to-end graph is built, timed and released at a time."""
+        args, world, dev, stream = self.args, self.world, self.dev, self.stream
+        h2d = sum(inputs[t][k].numel() * inputs[t][k].element_size()
+                  for t in tokens for k in ("hidden_states", "topk_ids", "topk_weights"))
+        d2h = sum(t * shape.hidden * 2 for t in tokens)
+        per_t = []
+        for t in tokens:
+            hi = {k: (v.pin_memory() if isinstance(v, torch.Tensor) else v) for k, v in inputs[t].items()}
+            ho = torch.empty((t, shape.hidden), dtype=torch.bfloat16).pin_memory()
+            d = {k: (torch.empty_like(v, device=dev) if isinstance(v, torch.Tensor) else v) for k, v in hi.items()}
+            for k in ("hidden_states", "topk_ids", "topk_weights"):
+                d[k].copy_(hi[k], non_blocking=True)
+            layer_call(d)
+            torch.cuda.synchronize()
+
+            def e2e_step():
+                for k in ("hidden_states", "topk_ids", "topk_weights"):
+                    d[k].copy_(hi[k], non_blocking=True)
+                ho.copy_(layer_call(d), non_blocking=True)
+
+            if world == 1:
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    e2e_step()
+            else:
+                g = _Eager(e2e_step)
+            evs = []
+            for i in range(max(1, args.warmup) + args.steps):
+                self.flush.zero_()
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(stream)
+                g.replay()
+                e1.record(stream)
+                if i >= max(1, args.warmup):
+                    evs.append((e0, e1))
+            torch.cuda.synchronize()
+            per_t.append(statistics.mean(a.elapsed_time(b) * 1e3 for a, b in evs))
+            del g, hi, ho, d
+        per_t = max_over_ranks(world, per_t)
+        return {"value": round(geomean(per_t), 3), "unit": "us/call", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "how": ("CUDA graph of " if world == 1 else "eager ") +
+                       "pinned-host->device copies, layer call, device->pinned-host copy",
+                "per_T_us": {str(t): round(v, 3) for t, v in zip(tokens, per_t)}}
+
+    def reference_style(self, graphs, tokens):
+        """The reference harness's way (TASK.md:66-70): L2 emptied by *reading* a buffer larger
+        than L2 (clean lines; the headline's write leaves dirty ones that the call must write
+        back), and the fixed cost of a graph replay, which that harness subtracts."""
+        args, dev = self.args, self.dev
         tiny = torch.zeros(1, dtype=torch.int32, device=dev)
         g_floor = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g_floor):
             tiny.add_(1)
-        floor_ev = timed({t: g_floor for t in tokens}, args.warmup + args.steps, read_flush=True)
-        rd_ev = timed(graphs, args.warmup + args.steps, read_flush=True)
+        floor_ev = self.timed({t: g_floor for t in tokens}, tokens, args.warmup + args.steps, read_flush=True)
+        rd_ev = self.timed(graphs, tokens, args.warmup + args.steps, read_flush=True)
         torch.cuda.synchronize()
         floor_us = statistics.mean(a.elapsed_time(b) * 1e3 for t in tokens for a, b in floor_ev[t][args.warmup:])
-        ref_style = {"floor_us": round(floor_us, 3),
-                     "us_read_flush": {t: round(statistics.mean(a.elapsed_time(b) * 1e3 for a, b in rd_ev[t][args.warmup:]), 3)
-                                       for t in tokens}}
+        rd = {t: statistics.mean(a.elapsed_time(b) * 1e3 for a, b in rd_ev[t][args.warmup:]) for t in tokens}
         del g_floor
+        return {"floor_us": round(floor_us, 3), "us_read_flush": {t: round(v, 3) for t, v in rd.items()}}
 
-    # Per-kernel times: the same calls, eager, with events recorded between the kernels (the
-    # 512 MiB flush in front of each call keeps the GPU behind the host, so no event waits on
-    # a launch). [0]->[1] route + gather (empty when GEMM1 routes), [1]->[2] GEMM1,
-    # [2]->[3] GEMM2, [3]->[4] combine.
-    stage_us = {t: [0.0, 0.0, 0.0, 0.0] for t in tokens}
-    if world == 1:
+    def stages(self, tokens, dev_in, state, outs):
+        """Per-kernel times: the same calls, eager, with events recorded between the kernels (the
+        512 MiB flush in front of each call keeps the GPU behind the host, so no event waits on
+        a launch). [0]->[1] route + gather (empty when GEMM1 routes), [1]->[2] GEMM1,
+        [2]->[3] GEMM2, [3]->[4] combine."""
         stage = {t: [] for t in tokens}
-        for i in range(args.steps):
+        for _ in range(self.args.steps):
             for t in tokens:
                 evs = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
-                flush.zero_()
-                pkg.kernel_fn(dev_in[t], state, out=outs[t], stage_events=evs)
+                self.flush.zero_()
+                self.pkg.kernel_fn(dev_in[t], state, out=outs[t], stage_events=evs)
                 stage[t].append(evs)
         torch.cuda.synchronize()
-        stage_us = {t: [statistics.mean(e[j].elapsed_time(e[j + 1]) * 1e3 for e in stage[t]) for j in range(4)]
-                    for t in tokens}
+        return {t: [statistics.mean(e[j].elapsed_time(e[j + 1]) * 1e3 for e in stage[t]) for j in range(4)]
+                for t in tokens}
 
-    per_t = [statistics.mean(a.elapsed_time(b) * 1e3 for a, b in ev[t]) for t in tokens]
-    per_t = max_over_ranks(world, per_t)
-    per_t_e2e = max_over_ranks(world, per_t_e2e)
-    flat = max_over_ranks(world, [v for t in tokens for v in stage_us[t]])
-    stage_us = {t: flat[4 * i:4 * i + 4] for i, t in enumerate(tokens)}
+    def rank_split(self, tokens, dev_in, moe):
+        """Each rank's time in its layer kernels and in the exchange (which includes the wait for
+        the slowest peer's signal), eager calls after an L2 flush, every rank in step."""
+        split = {t: [] for t in tokens}
+        for _ in range(self.args.steps):
+            for t in tokens:
+                evs = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+                self.flush.zero_()
+                barrier(self.world)
+                moe.forward_replicated(dev_in[t], stage_events=evs)
+                split[t].append(evs)
+        torch.cuda.synchronize()
+        flat = []
+        for t in tokens:
+            flat += [statistics.mean(e[0].elapsed_time(e[1]) * 1e3 for e in split[t]),
+                     statistics.mean(e[1].elapsed_time(e[2]) * 1e3 for e in split[t])]
+        per_rank = gather_ranks(self.world, flat)
+        return {str(t): {"layer_us": [round(r[2 * i], 2) for r in per_rank],
+                         "exchange_us": [round(r[2 * i + 1], 2) for r in per_rank],
+                         "exchange_mode": moe.exchange_mode(t * dev_in[t]["hidden_states"].shape[1])}
+                for i, t in enumerate(tokens)}
 
+    # -- rows -------------------------------------------------------------------------------
+
+    def rows(self, res):
+        """Per token count: time, algorithmic bytes and FLOPs, HBM fraction, launch plan and,
+        on one GPU, the per-kernel split; plus the dominant kernel's roofline aggregate."""
+        shape, tokens, world, traffic, _lib = res["shape"], res["tokens"], self.world, self.traffic, self._lib
+        pk = peaks()
+        dims = (shape.local_start, shape.n_local, shape.hidden, shape.inter)
+        stage_us = res.get("stage_us", {})
+        per_rows, dom_bytes, dom_time, launches = [], 0.0, 0.0, 0
+        for t, us in zip(tokens, res["per_t"]):
+            ids = res["inputs"][t]["topk_ids"].numpy()
+            b = traffic.layer_bytes(ids, *dims)
+            f = traffic.layer_flops(ids, *dims)
+            plan = _lib.launch_plan(t, shape.top_k, res["n_local"], shape.hidden, shape.inter)
+            launches += plan["launches"] + (1 if world > 1 else 0)   # + the exchange kernel
+            gbs = b / (us * 1e-6) / 1e9
+            row = {"T": t, "us": round(us, 3), "bytes": b, "flops": f, "GBps": round(gbs, 1),
+                   "hbm_frac": round(gbs / (pk["hbm_gbs"] * world), 4),
+                   "roofline_us": round(max(b / (pk["hbm_gbs"] * world) / 1e3,
+                                            f / (pk["bf16_tflops"] * world) / 1e6), 3),
+                   "launches": plan["launches"], "n_box": plan["n_box"], "path": plan["path"]}
+            if "ref_style" in res:
+                rd = res["ref_style"]["us_read_flush"][t]
+                row.update({"us_read_flush": rd,
+                            "us_read_flush_minus_floor": round(rd - res["ref_style"]["floor_us"], 3)})
+            if t in stage_us:
+                pre, k1, k2, comb = stage_us[t]
+                if plan["fused"]:
+                    row.update({"kernels_us": {"layer": round(k1, 3)},
+                                "layer_kernel_GBps": round(b / (k1 * 1e-6) / 1e9, 1)})
+                    dom_bytes += b
+                    dom_time += k1
+                else:
+                    b1 = traffic.gemm1_bytes(ids, *dims)
+                    b2 = traffic.gemm2_bytes(ids, *dims)
+                    row.update({"kernels_us": {"route_gather": round(pre, 3), "gemm1": round(k1, 3),
+                                               "gemm2": round(k2, 3), "combine": round(comb, 3)},
+                                "gemm1_GBps": round(b1 / (k1 * 1e-6) / 1e9, 1),
+                                "gemm2_GBps": round(b2 / (k2 * 1e-6) / 1e9, 1)})
+                    dom_bytes += b1
+                    dom_time += k1
+            if "rank_split" in res:
+                row["ranks"] = res["rank_split"][str(t)]
+            per_rows.append(row)
+        return per_rows, dom_bytes, dom_time, launches
+
+
+def traffic_record(name):
+    """ncu DRAM bytes per launch of the dominant kernel for this workload, if recorded."""
+    if not TRAFFIC_FILE.exists():
+        return None
+    return json.loads(TRAFFIC_FILE.read_text()).get(name)
+
+
+def run_muse(args, world, rank, local):
+    b = Bench(args, world, rank, local)
+    shape, tokens = sweep(b.synth, args.workload, args.tokens)
+    res = b.measure(args.workload, tokens, full=True)
+    per_rows, dom_bytes, dom_time, launches = b.rows(res)
+    per_t = res["per_t"]
     pk = peaks()
-    dims = (shape.local_start, shape.n_local, shape.hidden, shape.inter)
-    per_rows = []
-    g1_bytes = g1_time = 0.0
-    launches_per_step = 0
-    for t, us in zip(tokens, per_t):
-        ids = inputs[t]["topk_ids"].numpy()
-        b = traffic.layer_bytes(ids, *dims)
-        f = traffic.layer_flops(ids, *dims)
-        b1 = traffic.gemm1_bytes(ids, *dims)
-        b2 = traffic.gemm2_bytes(ids, *dims)
-        pre, k1, k2, comb = stage_us[t]
-        plan = _lib.launch_plan(t, shape.top_k, len(experts), shape.hidden, shape.inter)
-        launches_per_step += plan["launches"] + (1 if world > 1 else 0)   # + the bf16 cast
-        fused = plan["fused"]
-        gbs = b / (us * 1e-6) / 1e9
-        # the dominant kernel: the single layer kernel of a fused call, else GEMM1
-        g1_bytes += b if fused else b1
-        g1_time += k1
-        row = {"T": t, "us": round(us, 3), "bytes": b, "flops": f, "GBps": round(gbs, 1),
-               "hbm_frac": round(gbs / (pk["hbm_gbs"] * world), 4),
-               "roofline_us": round(max(b / (pk["hbm_gbs"] * world) / 1e3,
-                                        f / (pk["bf16_tflops"] * world) / 1e6), 3),
-               "launches": plan["launches"], "n_box": plan["n_box"], "path": plan["path"]}
-        if ref_style:
-            rd = ref_style["us_read_flush"][t]
-            row.update({"us_read_flush": rd, "us_read_flush_minus_floor": round(rd - ref_style["floor_us"], 3)})
-        if world == 1 and fused:   # per-kernel event times (single-GPU calls only)
-            row.update({"kernels_us": {"layer": round(k1, 3)},
-                        "layer_kernel_GBps": round(b / (k1 * 1e-6) / 1e9, 1)})
-        elif world == 1:
-            row.update({"kernels_us": {"route_gather": round(pre, 3), "gemm1": round(k1, 3),
-                                       "gemm2": round(k2, 3), "combine": round(comb, 3)},
-                        "gemm1_GBps": round(b1 / (k1 * 1e-6) / 1e9, 1),
-                        "gemm2_GBps": round(b2 / (k2 * 1e-6) / 1e9, 1)})
-        per_rows.append(row)
     if world == 1:
-        achieved = g1_bytes / (g1_time * 1e-6) / 1e9
+        achieved = dom_bytes / (dom_time * 1e-6) / 1e9
         roof_kernel = ("expert_gemm_tc launch of each call's dominant kernel (the single fused "
                        "layer kernel for decode batches, else GEMM1): algorithmic bytes per launch / "
                        "mean CUDA-event duration, summed over the token sweep")
@@ -497,39 +676,49 @@ def run_muse(args, world, rank, local):
         roof_kernel = (f"whole expert-parallel layer call over {world} GPUs (local layer kernels + "
                        f"peer-memory exchange), sweep aggregate, against {world} x HBM peak")
         roof_peak = pk["hbm_gbs"] * world
+    tr = traffic_record(args.workload) if world == 1 else None
     line = {
-        "metric": metric_name(args), "value": round(geomean(per_t), 3), "unit": "us/call",
+        "metric": metric_name(args.workload), "value": round(geomean(per_t), 3), "unit": "us/call",
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(sum(per_t) / 1e3, 5), "higher_is_better": False,
-        "scaling": "strong" if world > 1 else "weak",
-        "vs_baseline": published_ratio(args, tokens, geomean(per_t)), "dtype": "bf16",
+        "scaling": "strong",   # the same calls at every N, the experts split N ways
+        "vs_baseline": published_ratio(args.workload, tokens, geomean(per_t)), "dtype": "bf16",
         "data": "synthetic (seeded; random-init NVFP4 weights)",
-        "config": config_block(args, shape, tokens),
+        "config": config_block(args.workload, shape, tokens, world),
         "per_T": per_rows,
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": roof_peak, "unit": "GB/s",
-                     "frac": round(achieved / roof_peak, 4), "traffic": None,
+                     "frac": round(achieved / roof_peak, 4),
+                     "traffic": tr["bytes_per_launch"] if tr else None,
                      "peak_source": pk["source"], "kernel": roof_kernel},
-        "e2e": {"value": round(geomean(per_t_e2e), 3), "unit": "us/call", "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h,
-                "how": ("CUDA graph of " if world == 1 else "eager ") +
-                       "pinned-host->device copies, layer call, device->pinned-host copy"},
-        "gpu_launches": launches_per_step * args.steps,
-        "clocks": clocks.summary(),
+        "e2e": res["e2e"],
+        "parity": res["parity"],
+        "gpu_launches": launches * args.steps,
+        "clocks": res["clocks"],
     }
-    if ref_style:
-        rd = [ref_style["us_read_flush"][t] for t in tokens]
+    if tr:
+        line["roofline"]["traffic_source"] = tr["source"]
+    if "ref_style" in res:
+        rd = [res["ref_style"]["us_read_flush"][t] for t in tokens]
+        fl = res["ref_style"]["floor_us"]
         line["reference_harness_style"] = {
             "how": "same graphs; L2 emptied by reading (not writing) 512 MiB before each replay; "
                    "floor = replay of a one-kernel graph after the same read",
-            "floor_us": ref_style["floor_us"], "value": round(geomean(rd), 3),
-            "value_minus_floor": round(geomean([v - ref_style["floor_us"] for v in rd]), 3)}
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(shape, tokens, w, inputs)
+            "floor_us": fl, "value": round(geomean(rd), 3),
+            "value_minus_floor": round(geomean([v - fl for v in rd]), 3)}
+    if "cpu_baseline" in res and rank == 0:
+        line["cpu_baseline"] = res["cpu_baseline"]
+    if world == 1 and not args.no_secondary and args.workload == DEFAULT_WORKLOAD and args.tokens is None:
+        s_shape, s_tokens = sweep(b.synth, SECONDARY_WORKLOAD, None)
+        sres = b.measure(SECONDARY_WORKLOAD, s_tokens, full=False)
+        s_rows, s_bytes, s_time, _ = b.rows(sres)
+        line["secondary"] = {SECONDARY_WORKLOAD: {
+            "config": config_block(SECONDARY_WORKLOAD, s_shape, s_tokens, world)["workload"],
+            "value": round(geomean(sres["per_t"]), 3), "unit": "us/call", "per_T": s_rows,
+            "dominant_kernel_hbm_frac": round(s_bytes / (s_time * 1e-6) / 1e9 / pk["hbm_gbs"], 4)}}
     if rank == 0:
         print(json.dumps(line), flush=True)
-    del graphs   # graphs go before the process group
-    torch.cuda.synchronize()
-    return 0
+    ok = res["parity"] is None or res["parity"]["ok"]
+    return 0 if ok else 3
 
 
 def main(argv=None):

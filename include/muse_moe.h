@@ -69,8 +69,11 @@ int muse_moe_workspace_offsets(int tokens, int top_k, int local_count, int hidde
                                size_t* offsets);
 
 /*
- * Sticky per-device status word of the kernels' bounded waits: 0, or the code of the first
- * role whose wait expired (then a call returned garbage). Synchronous: copies from the device
+ * Sticky per-device status word of the kernels' bounded waits: 0, or the code of the last
+ * failure (then a call returned garbage): 1-4 a wait of the expert GEMM's producer / MMA /
+ * epilogue / dequantiser role expired, 5 the single launch's combine waited in vain for its
+ * rows, 6 an expert-parallel exchange waited in vain for a peer, 7 an exchange found the
+ * device's generation parity different from the caller's. Synchronous: copies from the device
  * on the current device; reset != 0 clears it. Not for use inside a captured graph.
  */
 int muse_moe_device_status(int* status, int reset);
@@ -160,25 +163,54 @@ int muse_moe_cast_bf16(const float* in, void* out, size_t n, muse_stream_t strea
  * The decode-layout exchange of an expert-parallel layer over NVLink peer memory:
  * out (bf16 [n], this rank) = sum over ranks r = 0 .. ranks-1, in that order, of rank r's share
  * (fp32 [n], its muse_moe_forward_partial output). shares0[r] / shares1[r] are rank r's two
- * share buffers and flags[r] its flag array (16 uint32, zero before the first call), all as
+ * share buffers and flags[r] its flag array (32 uint32, zero before the first call), all as
  * device addresses valid on this GPU (peer mappings of every rank's symmetric buffers, this
  * rank's own included). The call's generation g = 1, 2, 3, ... is counted on the device (so a
  * captured graph stays valid); call g reads the buffers of parity g & 1, so the caller writes
- * its share of the g-th call into shares{g & 1}[rank]. Waits for the peers are bounded (~1 s);
- * on expiry the output is left untouched and muse_moe_device_status reports 6. Replaces the
- * all-reduce that sums the ep8 ranks' partial outputs (reference.py:18-22, TASK.md:29 run one
- * rank per GPU).
+ * its share of the g-th call into shares{g & 1}[rank]. Waits for the peers are bounded (1 s);
+ * on expiry muse_moe_device_status reports 6 (see muse_moe_peer_exchange_bf16 for what a
+ * failure leaves behind). muse_moe_peer_exchange_bf16 in mode 0, without a parity check.
+ * Replaces the all-reduce that sums the ep8 ranks' partial outputs (reference.py:18-22,
+ * TASK.md:29 run one rank per GPU).
  */
 int muse_moe_peer_allreduce_bf16(const uint64_t* shares0, const uint64_t* shares1,
                                  const uint64_t* flags, int ranks, int rank, size_t n, void* out,
                                  muse_stream_t stream);
 
 /*
+ * The expert-parallel exchange with every option (the two calls below are shorthands for it).
+ * Sums the ranks' fp32 shares (shares0[r] / shares1[r], each of n elements, rank r's muse_moe_
+ * forward_partial output; parity g & 1 for the g-th call) in rank order, casts to bf16, and:
+ *   mode 0  all-reduce, one round: every rank reads every rank's whole share (R * n fp32 over
+ *           NVLink per rank) -- fewest synchronisations, for small shares;
+ *   mode 1  reduce-scatter: out (bf16 [n / ranks]) = this rank's slice of the sum (n a multiple
+ *           of 8 * ranks);
+ *   mode 2  all-reduce, two rounds: each rank sums only its 1/R slice (reads R * n / R fp32),
+ *           writes it to out and to its bf16 staging buffer staging[r] (n bf16, symmetric like the
+ *           shares), and after a second round of flags copies every other rank's slice from that
+ *           rank's staging buffer (n bf16 in all): the reduce-scatter + all-gather of the decode
+ *           exchange, for large shares. Launched cooperatively.
+ * flags[r]: rank r's flag array, 32 uint32, zero before the first call (and again before reuse
+ * after a failure). expect_parity: 0 or 1 = the parity of the buffer the caller wrote this call's
+ * share into; if the device's generation disagrees the call does nothing and the device status
+ * becomes 7. -1 skips the check. timeout_us bounds every wait for the peers (0 = 1 s); on expiry
+ * the device status becomes 6, the output is unspecified and the generation is not advanced --
+ * the ranks are then out of step and the flag arrays must be re-created (zeroed, then a barrier
+ * of all ranks) before the next call. All ranks produce identical bits. Replaces the all-reduce
+ * (decode) or reduce-scatter (prefill) that sums the ep ranks' partial outputs
+ * (reference.py:18-22, TASK.md:29: one rank per GPU).
+ */
+int muse_moe_peer_exchange_bf16(const uint64_t* shares0, const uint64_t* shares1,
+                                const uint64_t* flags, const uint64_t* staging, int ranks, int rank,
+                                size_t n, int mode, int expect_parity, long long timeout_us,
+                                void* out, muse_stream_t stream);
+
+/*
  * The prefill-layout exchange (tokens split over the ranks, ranks x n_per_rank elements in every
  * share): out (bf16 [n_per_rank], this rank) = sum over ranks r, in order, of elements
  * [rank * n_per_rank, (rank + 1) * n_per_rank) of rank r's share -- this rank's tokens. Same
  * buffers, flags, generation count and bounded waits as muse_moe_peer_allreduce_bf16 (the two
- * calls share one generation sequence). Replaces the reduce-scatter that returns each rank the
+ * calls share one generation sequence); muse_moe_peer_exchange_bf16 in mode 1. Replaces the reduce-scatter that returns each rank the
  * sum for its own tokens (reference.py:18-22, TASK.md:29).
  */
 int muse_moe_peer_reduce_scatter_bf16(const uint64_t* shares0, const uint64_t* shares1,
@@ -208,8 +240,11 @@ int muse_moe_forward_profiled(const void* x, const int32_t* topk_ids, const floa
  *   plan[3] 2: the whole layer in one cooperative launch after a memset of its counters
  *              (T*K <= 128 and token tile <= 32); 1: GEMM1 routes and gathers x in its own
  *              prologue, then GEMM2 and the combine (T*K <= 1024, token tile <= 32);
- *           0: route, gather, GEMM1, GEMM2, combine.
- * No counterpart in the reference; a diagnostic for benchmarks and tests.
+ *           0: route, gather, GEMM1, GEMM2, combine;
+ *   plan[4] 1 if the expert GEMMs run pair-tile items (each dequantised weight chunk feeds two
+ *           128-token tiles; prefill batches averaging >= 128 pairs per local expert), else 0.
+ * plan has room for 5 ints. No counterpart in the reference; a diagnostic for benchmarks and
+ * tests.
  */
 int muse_moe_launch_plan(int tokens, int top_k, int local_count, int hidden, int inter,
                          int* plan);
@@ -225,9 +260,11 @@ int muse_moe_launch_plan(int tokens, int top_k, int local_count, int hidden, int
  *   - Calls needing more than 32 MiB of scratch (muse_moe_workspace_size) are refused with
  *     MUSE_ERR_SCRATCH_LIMIT before any launch; decode-sized batches fit (top-8: up to 87
  *     tokens at H = 7168, I = 2048; up to 297 at H = 2048, I = 768).
- *   - A device holds the 32 MiB from the first call on it until the process exits. That first
- *     call looks up the array's device address, with the device current; make it before any
- *     stream capture.
+ *   - A device holds the 32 MiB from the first call on it until the process exits. Every call
+ *     looks the array's device address up on the current device (so a device reset, which may
+ *     move it, is followed); a call made while its stream is being captured reuses the address
+ *     of the last call on that device, so make one call on the device before capturing (a first
+ *     call inside a capture returns MUSE_ERR_INVALID_ARGUMENT), and capture again after a reset.
  *   - All calls on a device share the array and it keeps the last call's contents. Nothing in
  *     it needs to start at zero (every value a call reads, the same call wrote first), but
  *     calls that overlap on the GPU race on it: serialise them.

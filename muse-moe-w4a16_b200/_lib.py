@@ -38,6 +38,9 @@ SIGNATURES: dict[str, tuple] = {
                                           ctypes.POINTER(ctypes.c_uint64), _I, _I, ctypes.c_size_t, _P, _P]),
     "muse_moe_peer_reduce_scatter_bf16": (_I, [ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
                                                ctypes.POINTER(ctypes.c_uint64), _I, _I, ctypes.c_size_t, _P, _P]),
+    "muse_moe_peer_exchange_bf16": (_I, [ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
+                                         ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
+                                         _I, _I, ctypes.c_size_t, _I, _I, ctypes.c_longlong, _P, _P]),
     "muse_moe_forward_noalloc": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I,
                                       _P, _P, _P, _P, _P, _P, _P, _P, _P]),
 }
@@ -124,7 +127,7 @@ def workspace_size(tokens: int, top_k: int, local_count: int, hidden: int, inter
 
 def launch_plan(tokens: int, top_k: int, local_count: int, hidden: int, inter: int) -> dict:
     """Kernels, token tile, stages and routing mode of one forward call (include/muse_moe.h)."""
-    arr = (ctypes.c_int * 4)()
+    arr = (ctypes.c_int * 5)()
     call("muse_moe_launch_plan", tokens, top_k, local_count, hidden, inter, arr)
     return {"launches": arr[0], "n_box": arr[1], "stages": arr[2], "path": int(arr[3]),
-            "fused": arr[3] == 2, "route_inline": arr[3] >= 1}
+            "fused": arr[3] == 2, "route_inline": arr[3] >= 1, "pair_tiles": bool(arr[4])}

@@ -48,15 +48,18 @@ def _stale(target: Path, deps: list[Path]) -> bool:
     return any(d.stat().st_mtime > t for d in deps)
 
 
-def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | None = None) -> Path:
-    """Compile every csrc/*.cu for sm_100a and link libmusemoe.so; returns its path."""
+def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | None = None,
+          out: Path | None = None, build_dir: Path | None = None) -> Path:
+    """Compile every csrc/*.cu for sm_100a and link libmusemoe.so (or `out`); returns its path.
+    A variant build (extra defines) keeps its objects in its own `build_dir`."""
     nvcc = nvcc_path()
-    BUILD_DIR.mkdir(exist_ok=True)
+    bdir = Path(build_dir) if build_dir else BUILD_DIR
+    bdir.mkdir(parents=True, exist_ok=True)
     headers = _headers()
     flags = NVCC_FLAGS + ARCH + (extra_flags or [])
     jobs = []
     for src in _sources():
-        obj = BUILD_DIR / (src.stem + ".o")
+        obj = bdir / (src.stem + ".o")
         if force or _stale(obj, [src, *headers, Path(__file__)]):
             jobs.append([nvcc, *flags, "-c", str(src), "-o", str(obj)])
 
@@ -71,8 +74,8 @@ def build(force: bool = False, verbose: bool = False, extra_flags: list[str] | N
 
     with cf.ThreadPoolExecutor(max_workers=max(1, os.cpu_count() or 1)) as ex:
         list(ex.map(run, jobs))
-    objs = [BUILD_DIR / (s.stem + ".o") for s in _sources()]
-    lib = PKG_DIR / LIB_NAME
+    objs = [bdir / (s.stem + ".o") for s in _sources()]
+    lib = Path(out) if out else PKG_DIR / LIB_NAME
     if force or jobs or _stale(lib, objs):
         run([nvcc, *ARCH, "-shared", "-o", str(lib), *map(str, objs)])
     return lib
@@ -83,9 +86,15 @@ def main(argv=None) -> int:
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true")
     ap.add_argument("--ptxas-v", action="store_true", help="print register/smem usage (-Xptxas -v)")
+    ap.add_argument("--trace", action="store_true",
+                    help="variant with per-role clock stamps (-DMUSE_TRACE); needs --out")
+    ap.add_argument("--out", default=None, help="library path of a variant build")
     a = ap.parse_args(argv)
-    lib = build(force=a.force or a.ptxas_v, verbose=a.verbose or a.ptxas_v,
-                extra_flags=["-Xptxas", "-v"] if a.ptxas_v else None)
+    flags = (["-Xptxas", "-v"] if a.ptxas_v else []) + (["-DMUSE_TRACE"] if a.trace else [])
+    if a.trace and not a.out:
+        ap.error("--trace builds a variant library: give --out")
+    lib = build(force=a.force or a.ptxas_v, verbose=a.verbose or a.ptxas_v, extra_flags=flags or None,
+                out=a.out, build_dir=(BUILD_DIR / "trace") if a.trace else None)
     print(lib)
     return 0
 

@@ -68,6 +68,14 @@ int pick_n_box(int tokens, int top_k, int local_count) {
   return n;
 }
 
+// Pair-tile items (one dequantised weight chunk feeds two 128-token tiles): when the batch
+// averages at least 128 pairs per local expert, i.e. most of its pairs sit in experts with two
+// or more full tiles (prefill); shapes only.
+bool use_pair_tiles(int tokens, int top_k, int local_count) {
+  return pick_n_box(tokens, top_k, local_count) == 128 &&
+         (long long)tokens * top_k >= 128LL * local_count;
+}
+
 // The single-launch (fused) path: decode batches of at most kMaxFusedPairs pairs with a small
 // token tile. Above that the separate route / gather / GEMM1 / GEMM2 / combine launches are
 // faster on B200 (measured at 256 pairs, E=128, H=2048, I=768: 116.7 vs 120.8 us).
@@ -217,15 +225,17 @@ int forward_impl(const void* x, const int32_t* topk_ids, const float* topk_weigh
   const int P = d.n_pairs();
   const int rows = (int)pair_rows(tokens, top_k);
   const int n_box = pick_n_box(tokens, top_k, local_count);
+  const int path = path_of(tokens, top_k, local_count);
+  const bool pair = path == 0 && use_pair_tiles(tokens, top_k, local_count);
   int b_stages = 0;
-  const int stages = pick_stages(n_box, &b_stages);
+  const int stages = pick_stages(n_box, pair, &b_stages);
   auto mark = [&](int i) -> int { return ev ? (int)cudaEventRecord(ev[i], st) : 0; };
 
   // Smallest batches: one cooperative launch does the whole layer -- routing in every CTA's
   // prologue, GEMM1 with x rows gathered straight from x, GEMM2 as soon as each token tile's
   // GEMM1 rows are in, and the combine. Decode batches up to kMaxInlinePairs: GEMM1 routes and
-  // gathers x itself, then GEMM2 and the combine. Larger: all five kernels.
-  const int path = path_of(tokens, top_k, local_count);
+  // gathers x itself, then GEMM2 and the combine. Larger: all five kernels (pair-tile items
+  // for prefill-sized batches).
 
   CUtensorMap tmap_xs, tmap_x, tmap_i;
   if ((rc = make_bf16_tmap(&tmap_xs, s.xs, rows, hidden, n_box))) return rc;
@@ -236,6 +246,7 @@ int forward_impl(const void* x, const int32_t* topk_ids, const float* topk_weigh
   g.offsets = s.offsets;
   g.n_local = local_count;
   g.n_box = n_box;
+  g.pair_tiles = pair;
   g.stages = stages;
   g.b_stages = b_stages;
   g.inter = s.inter;
@@ -287,7 +298,6 @@ int forward_impl(const void* x, const int32_t* topk_ids, const float* topk_weigh
     g.ph[1] = gemm2;
     g.route_inline = 1;
     g.fused = 1;
-    g.combine_target = 4 * gemm2.m_tiles;
     g.tokens = tokens;
     g.hidden = hidden;
     g.topk_weights = topk_weights;
@@ -385,10 +395,12 @@ extern "C" int muse_moe_launch_plan(int tokens, int top_k, int local_count, int 
   if (rc) return rc;
   const int n_box = pick_n_box(tokens, top_k, local_count);
   const int path = path_of(tokens, top_k, local_count);
+  const bool pair = path == 0 && use_pair_tiles(tokens, top_k, local_count);
   plan[0] = tokens == 0 ? 0 : (path == 2 ? 1 : path == 1 ? 3 : 5);
   plan[1] = n_box;
   int b_stages = 0;
-  plan[2] = pick_stages(n_box, &b_stages);
+  plan[2] = pick_stages(n_box, pair, &b_stages);
   plan[3] = path;
+  plan[4] = pair;
   return MUSE_OK;
 }

@@ -32,6 +32,7 @@
 #include "layout.cuh"
 #include "ptx.cuh"
 #include "route.cuh"
+#include "trace.cuh"
 
 namespace muse {
 
@@ -72,8 +73,8 @@ struct PipeCtl {
   uint64_t b_empty[kMaxStages];
   uint64_t a_full[kMaxABuf];
   uint64_t a_empty[kMaxABuf];
-  uint64_t acc_full[2];
-  uint64_t acc_empty[2];
+  uint64_t acc_full[3];
+  uint64_t acc_empty[3];
   uint64_t drain;
 };
 
@@ -81,7 +82,7 @@ struct SharedCtl {
   PipeCtl pipe[kMaxPipes];
   uint32_t tmem_base;
   int tile_warp_sum[8];              // token tiles of experts [32w, 32w + 32)
-  int tile_prefix[kMaxExperts + 1];  // cumulative token tiles per expert
+  int tile_prefix[kMaxExperts + 1];  // cumulative item columns per expert (token tiles, or pairs of them)
   int ntiles[kMaxExperts];           // token tiles per expert
   uint32_t scale_lut[256];           // e4m3 byte -> bf16x2 (sf * 2^60, sf * 2^60)
   int offs[kMaxExperts + 1];         // route_inline: expert ranges of the pair rows
@@ -96,28 +97,35 @@ struct Geo {
   int Sw, Sb;         // weight / activation ring depths per pipeline
   int n_box;          // token tile = MMA N
   int n_a, n_acc;     // A buffers and accumulators per pipeline
-  uint32_t b_bytes;   // one activation slot: two 64-column boxes of n_box rows
+  uint32_t b_bytes;   // one activation slot: two 64-column boxes of n_box rows per token tile
   uint32_t pipe_bytes;
 };
+// Items of the pair-tile variant cover up to two token tiles of one expert: every dequantised
+// A chunk feeds two MMAs (one per tile), so the in-register conversion is done once per 2 x
+// n_box tokens. One pipeline, three accumulator slots of n_box columns (an item takes one or
+// two of them, so the epilogue of one tile overlaps the next item's MMAs), two A buffers.
+constexpr int kPairAccSlots = 3;
 constexpr uint32_t kWStageBytes = kTileCodeBytes + kTileScaleBytes;  // 9 KiB, 1 KiB multiple
 
-__host__ __device__ inline Geo make_geo(int pipe_cols, int n_box, int w_stages, int b_stages) {
+__host__ __device__ inline Geo make_geo(int pipe_cols, int n_box, int w_stages, int b_stages, bool pair) {
   Geo g;
   g.Sw = w_stages;
   g.Sb = b_stages;
   g.n_box = n_box;
-  g.n_acc = 2 * n_box <= pipe_cols / 2 ? 2 : 1;
+  g.n_acc = pair ? kPairAccSlots : (2 * n_box <= pipe_cols / 2 ? 2 : 1);
   g.n_a = (pipe_cols - g.n_acc * n_box) / kACols;
   if (g.n_a > kMaxABuf) g.n_a = kMaxABuf;
-  g.b_bytes = 2u * n_box * 128u;
+  g.b_bytes = (pair ? 4u : 2u) * n_box * 128u;
   g.pipe_bytes = w_stages * kWStageBytes + b_stages * g.b_bytes;
   return g;
 }
 
 // One work item: phase (GEMM), expert, 128-row weight tile m, token tile n (rows row0 ..
-// row0 + nvalid of the expert-grouped pairs), and the token tile's index over all experts.
+// row0 + nvalid of the expert-grouped pairs), and the token tile's index over all experts; in
+// the pair-tile variant nt = 2 when the item also covers tile n + 1 (nvalid1 rows from
+// row0 + n_box), else 1.
 struct Item {
-  int ph, e, m, n, row0, nvalid, tile;
+  int ph, e, m, n, row0, nvalid, tile, nt, nvalid1;
 };
 
 // Position in a ring of `size` slots: slot index and the parity of the slot's current use.
@@ -130,8 +138,10 @@ struct Ring {
   }
 };
 
-// Items are numbered phase by phase: phase 0 has tiles x ph[0].m_tiles items (n0), then phase
-// 1. Inside a phase, expert e owns items [tile_prefix[e] * m_tiles, tile_prefix[e + 1] * m_tiles).
+// Items are numbered phase by phase: phase 0 has cols x ph[0].m_tiles items (n0), then phase
+// 1. Inside a phase, expert e owns items [tile_prefix[e] * m_tiles, tile_prefix[e + 1] * m_tiles),
+// m-tile major: item column c of weight tile m is token tile c (or tiles 2c, 2c + 1 with kPair).
+template <bool kPair = false>
 __device__ __forceinline__ Item decode_item(const SharedCtl& c, const int32_t* offsets, int it, int n0,
                                             int n_local, int n_box, int mt0, int mt1) {
   Item r;
@@ -145,13 +155,16 @@ __device__ __forceinline__ Item decode_item(const SharedCtl& c, const int32_t* o
   }
   r.e = lo;
   const int local = it - c.tile_prefix[lo] * mt;
-  const int nt = c.ntiles[lo];
-  r.m = local / nt;
-  r.n = local - r.m * nt;
-  r.tile = c.tile_prefix[lo] + r.n;
+  const int cols = c.tile_prefix[lo + 1] - c.tile_prefix[lo];
+  r.m = local / cols;
+  const int col = local - r.m * cols;
+  r.n = kPair ? 2 * col : col;
+  r.tile = c.tile_prefix[lo] + col;
   const int begin = offsets[lo], cnt = offsets[lo + 1] - begin;
   r.row0 = begin + r.n * n_box;
   r.nvalid = min(n_box, cnt - r.n * n_box);
+  r.nt = kPair && (r.n + 1) * n_box < cnt ? 2 : 1;
+  r.nvalid1 = r.nt == 2 ? min(n_box, cnt - (r.n + 1) * n_box) : 0;
   return r;
 }
 
@@ -182,47 +195,66 @@ __device__ __forceinline__ void record_error(int* flag, int code) {
 
 // The layer's combine for the tokens of this CTA (fused launches): out[t] = sum over t's local
 // slots, in ascending expert order, of topk_weight * rsqrt(mean(ypart^2) + eps) * ypart, fp32,
-// then bf16 (or fp32 for an expert-parallel share). Rows are waited for through the GEMM2
-// tile counters. Restates reference.py:88-90,106-107 with combine.cu's arithmetic.
-__device__ __forceinline__ void combine_tokens(SharedCtl& ctl, const GemmArgs& a, int n_local, int n_box) {
+// then bf16 (or fp32 for an expert-parallel share). Restates reference.py:88-90,106-107 with
+// combine.cu's arithmetic. A token's slots are found and ordered from the routing tables before
+// the rows exist; then one wait on the GEMM2 completion counter (every epilogue warp of every
+// CTA adds 1 after its last item), and the rows' sums of squares and values are read together.
+__device__ __forceinline__ void combine_tokens(SharedCtl& ctl, const GemmArgs& a, int n_local) {
   const int K = a.top_k, H = a.hidden;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total_rows = ctl.offs[n_local];
+  bool waited = false;
   for (int t = blockIdx.x; t < a.tokens; t += gridDim.x) {
-    if (threadIdx.x < K) ctl.c_row[threadIdx.x] = -1;
+    if (threadIdx.x < K) {
+      ctl.c_row[threadIdx.x] = -1;
+      ctl.c_key[threadIdx.x] = a.ids[t * K + threadIdx.x];
+      ctl.c_scoef[threadIdx.x] = a.topk_weights[t * K + threadIdx.x];   // slot weights for now
+    }
     __syncthreads();
     for (int r = threadIdx.x; r < total_rows; r += blockDim.x)
       if (ctl.order[r] == t) ctl.c_row[ctl.slot_of_row[r]] = r;
     __syncthreads();
-    if (warp < K) {
-      const int sl = warp;
-      const int r = ctl.c_row[sl];
-      float coef = 0.f;
-      if (r >= 0) {
-        int lo = 0, hi = n_local;  // expert of row r: largest e with offs[e] <= r
-        while (hi - lo > 1) {
-          const int mid = (lo + hi) >> 1;
-          if (ctl.offs[mid] <= r) lo = mid; else hi = mid;
-        }
-        const int tile = ctl.tile_prefix[lo] + (r - ctl.offs[lo]) / n_box;
-        const bool ready = __all_sync(0xffffffffu, lane == 0 ? ptx::wait_counter(a.ph[1].signal + tile,
-                                                                                 a.combine_target)
-                                                             : true);
-        if (!ready && lane == 0) record_error(a.error_flag, 5);
-        coef = post_norm_coef(a.ssq + (size_t)r * (H >> 5), H, a.topk_weights[t * K + sl]);
-      }
-      if (lane == 0) {
-        ctl.c_coef[sl] = coef;
-        ctl.c_key[sl] = a.ids[t * K + sl];
-      }
+    if (threadIdx.x == 0) {
+      ctl.c_n = sort_local_slots(ctl.c_row, ctl.c_key, ctl.c_scoef, K, ctl.c_order, ctl.c_srow, ctl.c_coef);
+      if (!waited && !ptx::wait_counter(a.ph[1].signal, 4 * (int)gridDim.x)) record_error(a.error_flag, 5);
     }
-    __syncthreads();
-    if (threadIdx.x == 0)
-      ctl.c_n = sort_local_slots(ctl.c_row, ctl.c_key, ctl.c_coef, K, ctl.c_order, ctl.c_srow, ctl.c_scoef);
+    waited = true;
     __syncthreads();
     const int n = ctl.c_n;
-    for (int h4 = threadIdx.x; h4 * 4 < H; h4 += blockDim.x) {
-      const float4 acc = weighted_rows(a.ypart, H, ctl.c_srow, ctl.c_scoef, n, h4);
+    if (warp < n) {   // sorted slot `warp`: its post-norm coefficient (c_coef holds its weight)
+      const float c = post_norm_coef(a.ssq + (size_t)ctl.c_srow[warp] * (H >> 5), H, ctl.c_coef[warp]);
+      if (lane == 0) ctl.c_scoef[warp] = c;
+    }
+    // The rows' values are loaded while the coefficients are being computed. Every thread makes
+    // the same number of passes (the barrier inside), and only those with a column group work.
+    for (int base4 = 0; base4 * 4 < H; base4 += blockDim.x) {
+      const int h4 = base4 + threadIdx.x;
+      const bool mine = h4 * 4 < H;
+      // the first eight rows are in flight across the barrier; more slots (top_k > 8) follow
+      float4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (mine && u < n) v[u] = __ldcg(reinterpret_cast<const float4*>(a.ypart + (size_t)ctl.c_srow[u] * H) + h4);
+      __syncthreads();
+      if (!mine) continue;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int u0 = 0; u0 < n; u0 += 8) {
+        if (u0 > 0) {
+#pragma unroll
+          for (int u = 0; u < 8; ++u)
+            if (u0 + u < n) v[u] = __ldcg(reinterpret_cast<const float4*>(a.ypart + (size_t)ctl.c_srow[u0 + u] * H) + h4);
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+          if (u0 + u < n) {
+            const float c = ctl.c_scoef[u0 + u];
+            acc.x = fmaf(c, v[u].x, acc.x);
+            acc.y = fmaf(c, v[u].y, acc.y);
+            acc.z = fmaf(c, v[u].z, acc.z);
+            acc.w = fmaf(c, v[u].w, acc.w);
+          }
+        }
+      }
       if (a.out_f32)
         reinterpret_cast<float4*>(static_cast<float*>(a.out) + (size_t)t * H)[h4] = acc;
       else
@@ -233,18 +265,20 @@ __device__ __forceinline__ void combine_tokens(SharedCtl& ctl, const GemmArgs& a
 }
 
 // kFused: the single-launch variant (two phases with cross-CTA tile counters, then the
-// combine). The plain variant leaves that code out of its loops.
-template <int P, int DW, bool kFused>
+// combine). The plain variant leaves that code out of its loops. kPair: items of up to two
+// token tiles (P = 1; see kPairAccSlots).
+template <int P, int DW, bool kFused, bool kPair>
 __global__ void __launch_bounds__(Roles<P, DW>::kThreads, 1)
 expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant__ CUtensorMap tmap_x,
                const __grid_constant__ CUtensorMap tmap_b2, const GemmArgs a) {
+  static_assert(!kPair || (P == 1 && !kFused), "pair-tile items: one pipeline, separate launches");
   using R = Roles<P, DW>;
   constexpr int kPipes = P;
   constexpr int kMmaWarp0 = R::kMmaWarp0, kEpiWarp0 = R::kEpiWarp0, kDeqWarp0 = R::kDeqWarp0;
   constexpr int kPipeCols = R::kPipeCols;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  const Geo geo = make_geo(kPipeCols, a.n_box, a.stages, a.b_stages);
+  const Geo geo = make_geo(kPipeCols, a.n_box, a.stages, a.b_stages, kPair);
   const int Sw = geo.Sw, Sb = geo.Sb, n_box = geo.n_box;
   SharedCtl& ctl = *reinterpret_cast<SharedCtl*>(smem + (size_t)kPipes * geo.pipe_bytes);
   // pipeline p: Sw weight slots [fp4 codes | scales], then Sb activation slots [box | box]
@@ -255,6 +289,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_local = a.n_local;
+  if (threadIdx.x == 0) MUSE_TRACE_ENTRY();
 
   // ---- set-up: barriers, scale table, work list, tensor memory
   if (threadIdx.x == 0) {
@@ -272,7 +307,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
         ptx::mbar_init(&pc.a_full[b], DW);
         ptx::mbar_init(&pc.a_empty[b], 1);
       }
-      for (int b = 0; b < 2; ++b) {
+      for (int b = 0; b < geo.n_acc; ++b) {
         ptx::mbar_init(&pc.acc_full[b], 1);
         ptx::mbar_init(&pc.acc_empty[b], 4);
       }
@@ -296,7 +331,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     }
     offs = ctl.offs;
   }
-  int incl = 0;  // token tiles of experts [32 * warp, threadIdx.x], threads < 256
+  int incl = 0;  // item columns of experts [32 * warp, threadIdx.x], threads < 256
   if (threadIdx.x < 256) {
     const float f = e4m3_to_float(threadIdx.x) * 1152921504606846976.0f;  // * 2^60
     const __nv_bfloat16 h = __float2bfloat16_rn(f);
@@ -308,7 +343,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     if (e < n_local) cnt = offs[e + 1] - offs[e];
     const int nt = (cnt + n_box - 1) / n_box;
     if (e < n_local) ctl.ntiles[e] = nt;
-    incl = nt;
+    incl = kPair ? (nt + 1) >> 1 : nt;
 #pragma unroll
     for (int d = 1; d < 32; d <<= 1) {
       const int o = __shfl_up_sync(0xffffffffu, incl, d);
@@ -339,9 +374,10 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     if (threadIdx.x == 0) ctl.tile_prefix[0] = 0;
   }
   __syncthreads();
+  if (threadIdx.x == 0) MUSE_TRACE_AT(2);
 
   const uint32_t tbase = ctl.tmem_base;
-  const int tiles = ctl.tile_prefix[n_local];
+  const int tiles = ctl.tile_prefix[n_local];       // item columns (token tiles, or pairs)
   const int mt0 = a.ph[0].m_tiles, mt1 = kFused && a.n_phases > 1 ? a.ph[1].m_tiles : 0;
   const int n0 = tiles * mt0;                       // items of phase 0
   const int total = n0 + tiles * mt1;               // all items of this launch
@@ -388,7 +424,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
         const int kcn = f.k_chunks, kstep = split ? kPipes : 1;
         const int kc0 = chunk_begin(p, jm, f, split);
         if (kc0 >= kcn) continue;
-        const Item t = decode_item(ctl, offs, it, n0, n_local, n_box, mt0, mt1);
+        const Item t = decode_item<kPair>(ctl, offs, it, n0, n_local, n_box, mt0, mt1);
         const size_t tile0 = ((size_t)t.e * f.m_tiles + t.m) * kcn;
         bool dep_ok = !kFused || f.wait_for == nullptr;
         for (int kc = kc0; kc < kcn; kc += kstep) {
@@ -402,6 +438,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
             ptx::bulk_g2s(wp, f.wq + (tile0 + kc) * kTileCodeBytes, kTileCodeBytes, &pc.w_full[ws.slot]);
             ptx::bulk_g2s(wp + kTileCodeBytes, f.wsf + (tile0 + kc) * kTileScaleBytes, kTileScaleBytes,
                           &pc.w_full[ws.slot]);
+            MUSE_TRACE_SEQ(trace::kTrW, p, w_issued);
           }
           ++w_issued;
           ws.next(Sw);
@@ -412,7 +449,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
               const int itl = blockIdx.x + (j + lane) * G;
               bool rdy = false;
               if (itl < total && itl >= n0) {
-                const Item tl = decode_item(ctl, offs, itl, n0, n_local, n_box, mt0, mt1);
+                const Item tl = decode_item<kPair>(ctl, offs, itl, n0, n_local, n_box, mt0, mt1);
                 rdy = ptx::ld_acquire_gpu(f.wait_for + tl.tile) >= f.wait_target;
               }
               dep_ready = __ballot_sync(0xffffffffu, rdy);
@@ -451,11 +488,16 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
               }
             }
           } else if (leader) {
+            // [tile 0: box | box][tile 1: box | box] (pair items), each box 64 columns x n_box rows
             const CUtensorMap* tm = f.b_source == 2 ? &tmap_b2 : &tmap_b;
-            ptx::mbar_arrive_expect_tx(bb, geo.b_bytes);
-            ptx::tma_load_2d(bp, tm, kc * kChunkK, t.row0, bb);
-            ptx::tma_load_2d(bp + n_box * 128, tm, kc * kChunkK + 64, t.row0, bb);
+            const uint32_t tile_bytes = 2u * n_box * 128u;
+            ptx::mbar_arrive_expect_tx(bb, t.nt * tile_bytes);
+            for (int h = 0; h < t.nt; ++h) {
+              ptx::tma_load_2d(bp + h * tile_bytes, tm, kc * kChunkK, t.row0 + h * n_box, bb);
+              ptx::tma_load_2d(bp + h * tile_bytes + n_box * 128, tm, kc * kChunkK + 64, t.row0 + h * n_box, bb);
+            }
           }
+          if (leader) MUSE_TRACE_SEQ(trace::kTrB, p, b_issued);
           ++b_issued;
           bs.next(Sb);
         }
@@ -496,6 +538,9 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
       const uint32_t stage_step = geo.b_bytes >> 4;              // descriptor units (16 B)
       const uint32_t atom_step = (uint32_t)(n_box * 128) >> 4;  // second 64-K box of a slot
       uint64_t desc_stage = desc_first;
+#ifdef MUSE_TRACE
+      int tr_c = 0;
+#endif
       int jm = 0;
       for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
         const int ph = phase_of(blockIdx.x + j * G);
@@ -507,15 +552,23 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
         // MMA width = the item's token rows rounded up to 16, not the whole tile: a partly
         // filled tile (the last of an expert, or an expert with few pairs) costs the tensor
         // core only its own columns
-        const Item t = decode_item(ctl, offs, blockIdx.x + j * G, n0, n_local, n_box, mt0, mt1);
+        const Item t = decode_item<kPair>(ctl, offs, blockIdx.x + j * G, n0, n_local, n_box, mt0, mt1);
         const uint32_t idesc = ptx::idesc_bf16_f32(kTileM, min(n_box, (t.nvalid + 15) & ~15));
         const int acc = accr.slot;
-        if (!__all_sync(0xffffffffu, ptx::mbar_wait_sleep(&pc.acc_empty[acc], accr.phase ^ 1))) {
+        // pair items: the second tile's accumulator is the ring's next slot
+        Ring acc2 = accr;
+        acc2.next(geo.n_acc);
+        const bool two = kPair && t.nt == 2;
+        const uint32_t idesc2 = two ? ptx::idesc_bf16_f32(kTileM, min(n_box, (t.nvalid1 + 15) & ~15)) : 0u;
+        if (!__all_sync(0xffffffffu, ptx::mbar_wait_sleep(&pc.acc_empty[acc], accr.phase ^ 1) &&
+                                         (!two || ptx::mbar_wait_sleep(&pc.acc_empty[acc2.slot], acc2.phase ^ 1)))) {
           ok = false;
           break;
         }
         ptx::tc_fence_after();
         const uint32_t d_tmem = acc_col0 + acc * n_box;
+        const uint32_t d_tmem2 = acc_col0 + acc2.slot * n_box;
+        const uint32_t tile_step = (2u * n_box * 128u) >> 4;   // second tile's boxes in a slot
         for (int kc = kc0; kc < kcn; kc += kstep) {
           const int s = st.slot;
           const int ab = ar.slot;
@@ -532,19 +585,30 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
             for (int kk = 0; kk < kChunkK / 16; ++kk) {
               const uint64_t bdesc = desc_stage + (uint64_t)((kk >> 2) * atom_step + (kk & 3) * 2);
               ptx::mma_bf16_ts(d_tmem, a_tmem + kk * 8, bdesc, idesc, (kc != kc0) | (kk != 0));
+              if (two) ptx::mma_bf16_ts(d_tmem2, a_tmem + kk * 8, bdesc + tile_step, idesc2, (kc != kc0) | (kk != 0));
             }
             ptx::mma_commit(&pc.b_empty[s]);
             ptx::mma_commit(&pc.a_empty[ab]);
+#ifdef MUSE_TRACE
+            MUSE_TRACE_SEQ(trace::kTrM, p, tr_c);
+#endif
           }
+#ifdef MUSE_TRACE
+          ++tr_c;
+#endif
           __syncwarp();
           ar.next(geo.n_a);
           st.next(Sb);
           desc_stage = st.slot == 0 ? desc_first : desc_stage + stage_step;
         }
         if (!ok) break;
-        if (leader) ptx::mma_commit(&pc.acc_full[acc]);
+        if (leader) {
+          ptx::mma_commit(&pc.acc_full[acc]);
+          if (two) ptx::mma_commit(&pc.acc_full[acc2.slot]);
+        }
         __syncwarp();
         accr.next(geo.n_acc);
+        if (two) accr.next(geo.n_acc);
       }
       if (!ok && leader) record_error(a.error_flag, 2);
       // all issued MMAs complete before tensor memory is released
@@ -561,7 +625,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     // Per-item constants (the item, its global scale, this lane's post-norm weight) are loaded
     // one item ahead, so their global-memory latency overlaps the previous item.
     auto item_consts = [&](int it, Item& t, float& gs, float& pnw) {
-      t = decode_item(ctl, offs, it, n0, n_local, n_box, mt0, mt1);
+      t = decode_item<kPair>(ctl, offs, it, n0, n_local, n_box, mt0, mt1);
       const PhaseArgs& f = a.ph[t.ph];
       gs = __ldg(f.gs + t.e);
       pnw = f.mode == 2 ? bf16_bits_to_float(__ldg(a.post_norm_w + kTileM * t.m + 32 * q + lane)) : 0.f;
@@ -569,129 +633,163 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     Item t_next;
     float gs_next = 0.f, pnw_next = 0.f;
     if (blockIdx.x < total) item_consts(blockIdx.x, t_next, gs_next, pnw_next);
+    // Single launch: this warp's GEMM1 rows are published once, after its last GEMM1 item (one
+    // GPU-scope fence, then a relaxed increment of each item's token-tile counter), and its
+    // GEMM2 rows once, after its last item (one increment of the completion counter). The warp
+    // barrier orders every lane's stores before lane 0's fence.
+    bool gemm1_published = !kFused || a.ph[0].signal == nullptr;
+    auto publish_gemm1 = [&](int j_end) {
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence();
+        for (int jj = 0; jj < j_end; ++jj) {
+          const Item ti = decode_item<kPair>(ctl, offs, blockIdx.x + jj * G, n0, n_local, n_box, mt0, mt1);
+          ptx::red_relaxed_gpu_add(a.ph[0].signal + ti.tile, 1);
+        }
+      }
+      __syncwarp();
+      gemm1_published = true;
+    };
     int jm = 0;
-    for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
+    int j = 0;
+    for (; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
+      if (!gemm1_published && blockIdx.x + j * G >= n0) publish_gemm1(j);
       const Item t = t_next;
       const float gs_item = gs_next, pnw_item = pnw_next;
       if (blockIdx.x + (j + 1) * G < total) item_consts(blockIdx.x + (j + 1) * G, t_next, gs_next, pnw_next);
       const PhaseArgs& f = a.ph[t.ph];
       const bool split = t.ph ? split1 : split0;
       const int kcn = f.k_chunks;
-      // accumulators of the participating pipelines
-      uint32_t taddr[kPipes];
-      int used = 0;
+      // a pair item's second token tile is a second accumulator, finished the same way
+      for (int tt = 0; tt < (kPair ? t.nt : 1); ++tt) {
+        const int row0 = t.row0 + tt * n_box;
+        const int nvalid = tt ? t.nvalid1 : t.nvalid;
+        // accumulators of the participating pipelines
+        uint32_t taddr[kPipes];
+        int used = 0;
 #pragma unroll
-      for (int p = 0; p < kPipes; ++p) {
-        if (chunk_begin(p, jm, f, split) >= kcn) continue;
-        if (!ptx::mbar_wait_sleep(&ctl.pipe[p].acc_full[accr[p].slot], accr[p].phase)) ok = false;
-        taddr[used++] = lane_base + p * kPipeCols + accr[p].slot * n_box;
-      }
-      if (!ok) break;
-      ptx::tc_fence_after();
-      const float gsc = gs_item * kUnscale;
-      if (f.mode == 1) {
-        const int jj = 64 * t.m + 16 * q + (lane & 15);  // intermediate index of this lane
-        for (int cb = 0; cb * 16 < t.nvalid; ++cb) {
-          float acc[16];
-          uint32_t v[16];
-          ptx::tmem_ld16(taddr[0] + cb * 16, v);
-          ptx::tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 16; ++c) acc[c] = __uint_as_float(v[c]);
-          for (int u = 1; u < used; ++u) {
-            ptx::tmem_ld16(taddr[u] + cb * 16, v);
+        for (int p = 0; p < kPipes; ++p) {
+          if (chunk_begin(p, jm, f, split) >= kcn) continue;
+          if (!ptx::mbar_wait_sleep(&ctl.pipe[p].acc_full[accr[p].slot], accr[p].phase)) ok = false;
+          taddr[used++] = lane_base + p * kPipeCols + accr[p].slot * n_box;
+        }
+        if (!ok) break;
+        ptx::tc_fence_after();
+        if (q == 0 && lane == 0) MUSE_TRACE_ITEM(trace::kTrE, j);
+        const float gsc = gs_item * kUnscale;
+        if (f.mode == 1) {
+          const int jj = 64 * t.m + 16 * q + (lane & 15);  // intermediate index of this lane
+          for (int cb = 0; cb * 16 < nvalid; ++cb) {
+            float acc[16];
+            uint32_t v[16];
+            ptx::tmem_ld16(taddr[0] + cb * 16, v);
             ptx::tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 16; ++c) acc[c] += __uint_as_float(v[c]);
-          }
-          // four columns at a time (independent chains the scheduler can overlap), only as many
-          // groups as the item has rows: the epilogue shares the issue slots of the dequantisers
-          const int ncols = min(16, t.nvalid - cb * 16);  // warp-uniform
+            for (int c = 0; c < 16; ++c) acc[c] = __uint_as_float(v[c]);
+            for (int u = 1; u < used; ++u) {
+              ptx::tmem_ld16(taddr[u] + cb * 16, v);
+              ptx::tmem_wait_ld();
 #pragma unroll
-          for (int c4 = 0; c4 < 16; c4 += 4) {
-            if (c4 >= ncols) break;
-            float act[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float mine = acc[c4 + k] * gsc;
-              const float other = __shfl_xor_sync(0xffffffffu, mine, 16);
-              act[k] = mine / (1.0f + __expf(-mine)) * other;  // lanes < 16: silu(gate) * up
+              for (int c = 0; c < 16; ++c) acc[c] += __uint_as_float(v[c]);
             }
-            if (lane < 16) {
+            // four columns at a time (independent chains the scheduler can overlap), only as many
+            // groups as the item has rows: the epilogue shares the issue slots of the dequantisers
+            const int ncols = min(16, nvalid - cb * 16);  // warp-uniform
+#pragma unroll
+            for (int c4 = 0; c4 < 16; c4 += 4) {
+              if (c4 >= ncols) break;
+              float act[4];
 #pragma unroll
               for (int k = 0; k < 4; ++k) {
-                if (c4 + k < ncols) {
-                  const __nv_bfloat16 hb = __float2bfloat16_rn(act[k]);
-                  a.inter[(size_t)(t.row0 + cb * 16 + c4 + k) * f.ld_out + jj] = *reinterpret_cast<const uint16_t*>(&hb);
+                const float mine = acc[c4 + k] * gsc;
+                const float other = __shfl_xor_sync(0xffffffffu, mine, 16);
+                // lanes < 16: silu(gate) * up; fast divide (2 ulp): the result is rounded to bf16
+                act[k] = __fdividef(mine, 1.0f + __expf(-mine)) * other;
+              }
+              if (lane < 16) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  if (c4 + k < ncols) {
+                    const __nv_bfloat16 hb = __float2bfloat16_rn(act[k]);
+                    a.inter[(size_t)(row0 + cb * 16 + c4 + k) * f.ld_out + jj] = *reinterpret_cast<const uint16_t*>(&hb);
+                  }
                 }
               }
             }
           }
-        }
-      } else {
-        const int h = kTileM * t.m + 32 * q + lane;  // output row of this lane
-        const float wn = gsc * (1.0f + pnw_item);
-        for (int cb = 0; cb * 16 < t.nvalid; ++cb) {
-          float acc[16];
-          uint32_t v[16];
-          ptx::tmem_ld16(taddr[0] + cb * 16, v);
-          ptx::tmem_wait_ld();
-#pragma unroll
-          for (int c = 0; c < 16; ++c) acc[c] = __uint_as_float(v[c]);
-          for (int u = 1; u < used; ++u) {
-            ptx::tmem_ld16(taddr[u] + cb * 16, v);
+        } else {
+          const int h = kTileM * t.m + 32 * q + lane;  // output row of this lane
+          const float wn = gsc * (1.0f + pnw_item);
+          for (int cb = 0; cb * 16 < nvalid; ++cb) {
+            float acc[16];
+            uint32_t v[16];
+            ptx::tmem_ld16(taddr[0] + cb * 16, v);
             ptx::tmem_wait_ld();
 #pragma unroll
-            for (int c = 0; c < 16; ++c) acc[c] += __uint_as_float(v[c]);
-          }
-          const int ncols = min(16, t.nvalid - cb * 16);  // warp-uniform
+            for (int c = 0; c < 16; ++c) acc[c] = __uint_as_float(v[c]);
+            for (int u = 1; u < used; ++u) {
+              ptx::tmem_ld16(taddr[u] + cb * 16, v);
+              ptx::tmem_wait_ld();
 #pragma unroll
-          for (int col = 0; col < 16; ++col) {
-            acc[col] *= wn;
-            if (col < ncols) a.ypart[(size_t)(t.row0 + cb * 16 + col) * f.ld_out + h] = acc[col];
-            acc[col] *= acc[col];
-          }
-          // Sum of squares of each column over the warp's 32 rows, all 16 columns at once: a
-          // transposed butterfly (each round halves the columns a lane keeps, 16 shuffles in
-          // all). It adds the same pairs as a per-column xor 16/8/4/2/1 reduction, so the sums
-          // are bit-identical to it; lanes 2c and 2c + 1 end with column c.
-#pragma unroll
-          for (int half = 8; half >= 1; half >>= 1) {
-            const bool up = lane & (2 * half);
-#pragma unroll
-            for (int i = 0; i < half; ++i) {
-              const float keep = up ? acc[half + i] : acc[i];
-              const float send = up ? acc[i] : acc[half + i];
-              acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2 * half);
+              for (int c = 0; c < 16; ++c) acc[c] += __uint_as_float(v[c]);
             }
+            const int ncols = min(16, nvalid - cb * 16);  // warp-uniform
+#pragma unroll
+            for (int col = 0; col < 16; ++col) {
+              acc[col] *= wn;
+              if (col < ncols) a.ypart[(size_t)(row0 + cb * 16 + col) * f.ld_out + h] = acc[col];
+              acc[col] *= acc[col];
+            }
+            // Sum of squares of each column over the warp's 32 rows, all 16 columns at once: a
+            // transposed butterfly (each round halves the columns a lane keeps, 16 shuffles in
+            // all). It adds the same pairs as a per-column xor 16/8/4/2/1 reduction, so the sums
+            // are bit-identical to it; lanes 2c and 2c + 1 end with column c.
+#pragma unroll
+            for (int half = 8; half >= 1; half >>= 1) {
+              const bool up = lane & (2 * half);
+#pragma unroll
+              for (int i = 0; i < half; ++i) {
+                const float keep = up ? acc[half + i] : acc[i];
+                const float send = up ? acc[i] : acc[half + i];
+                acc[i] = keep + __shfl_xor_sync(0xffffffffu, send, 2 * half);
+              }
+            }
+            acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 1);
+            const int c = (lane >> 1) & 15;
+            if (!(lane & 1) && c < ncols)
+              a.ssq[(size_t)(row0 + cb * 16 + c) * (f.ld_out >> 5) + (h >> 5)] = acc[0];
           }
-          acc[0] += __shfl_xor_sync(0xffffffffu, acc[0], 1);
-          const int c = (lane >> 1) & 15;
-          if (!(lane & 1) && c < ncols)
-            a.ssq[(size_t)(t.row0 + cb * 16 + c) * (f.ld_out >> 5) + (h >> 5)] = acc[0];
+        }
+        ptx::tc_fence_before();
+        if (q == 0 && lane == 0) MUSE_TRACE_ITEM(trace::kTrE + trace::kTrJ, j);
+        __syncwarp();
+#pragma unroll
+        for (int p = 0; p < kPipes; ++p) {
+          if (chunk_begin(p, jm, f, split) >= kcn) continue;
+          if (lane == 0) ptx::mbar_arrive(&ctl.pipe[p].acc_empty[accr[p].slot]);
+          accr[p].next(geo.n_acc);
         }
       }
-      ptx::tc_fence_before();
-      if (kFused && f.signal) {
-        // publish this warp's rows of the item: the warp barrier orders every lane's stores
-        // before lane 0's release, which makes them visible GPU-wide before the count
+    }
+    if (kFused && ok) {
+      if (!gemm1_published) publish_gemm1(j);
+      if (a.ph[1].signal) {
         __syncwarp();
-        if (lane == 0) ptx::red_release_gpu_add(f.signal + t.tile, 1);
-      }
-      __syncwarp();
-#pragma unroll
-      for (int p = 0; p < kPipes; ++p) {
-        if (chunk_begin(p, jm, f, split) >= kcn) continue;
-        if (lane == 0) ptx::mbar_arrive(&ctl.pipe[p].acc_empty[accr[p].slot]);
-        accr[p].next(geo.n_acc);
+        if (lane == 0) {
+          __threadfence();
+          ptx::red_relaxed_gpu_add(a.ph[1].signal, 1);
+        }
       }
     }
     if (!ok && lane == 0) record_error(a.error_flag, 3);
   } else {
     // ------------------------------------------------------------------ dequantisers
-    // Each chunk's codes and scale-table entries are read into registers right after the
-    // previous chunk is handed to the MMA, and the A buffer is waited for only once the first
-    // 16 columns are converted.
+    // A chunk is converted in 16-column groups (32 elements of this thread's row). The shared-
+    // memory reads of group g + 1 -- its 16 code bytes and its two scale-table entries -- are
+    // issued before group g is converted, so their latency hides behind the arithmetic; the
+    // reads of the next chunk's first group are issued during the last group whenever that
+    // weight tile has already landed. A weight slot is handed back as soon as its last bytes
+    // are in registers, and the A buffer is waited for only once the first group is converted.
     const int p = (warp - kDeqWarp0) / DW;
     PipeCtl& pc = ctl.pipe[p];
     const int q = warp & 3;                  // TMEM lane quarter
@@ -699,7 +797,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     const int row = 32 * q + lane;           // weight row of this thread
     const uint32_t lane_col0 = tbase + ((uint32_t)(32 * q) << 16) + p * kPipeCols;
     const uint32_t m16 = a.mul16, m64 = a.mul64;
-    constexpr int kHalves = DW == 8 ? 1 : 2;  // halves of the chunk this warp converts
+    constexpr int kGroups = DW == 8 ? 2 : 4;  // 16-column groups of a chunk this warp converts
     bool ok = true;
     Ring st, ar;
     // this pipeline's chunks in order: item j (jm = j % P), chunk kc of it
@@ -719,58 +817,100 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
       }
       return true;
     };
-    uint4 cw[2 * kHalves];
-    uint32_t sc[4 * kHalves];
-    // Wait for the next weight slot, read this row's code and scale bytes, hand the slot back
-    // to the producer, then look the scales up.
-    auto fetch = [&]() -> bool {
-      if (!ptx::mbar_wait_sleep(&pc.w_full[st.slot], st.phase)) return false;
-      const uint8_t* wp = w_slot(p, st.slot);
-      const uint8_t* arow = wp + row * kRowCodeBytes;
-#pragma unroll
-      for (int c = 0; c < 2 * kHalves; ++c)
-        cw[c] = *reinterpret_cast<const uint4*>(arow + 16 * code_slot(row, 2 * hsel + c));
-      const uint2 sfw = *reinterpret_cast<const uint2*>(wp + kTileCodeBytes + row * kRowScaleBytes);
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&pc.w_empty[st.slot]);
-      st.next(Sw);
-#pragma unroll
-      for (int hh = 0; hh < kHalves; ++hh) {
-        const uint32_t sw = hsel + hh ? sfw.y : sfw.x;  // the 4 scale bytes of these 64 elements
-#pragma unroll
-        for (int i = 0; i < 4; ++i) sc[4 * hh + i] = ctl.scale_lut[__byte_perm(sw, 0, 0x4440 + i)];
-      }
-      return true;
+#ifdef MUSE_TRACE
+    int tr_c = 0;
+#endif
+    // Group g's 16 code bytes of this row in weight slot `slot`.
+    auto load_codes = [&](int slot, int g) -> uint4 {
+      return *reinterpret_cast<const uint4*>(w_slot(p, slot) + row * kRowCodeBytes +
+                                             16 * code_slot(row, 2 * hsel + g));
+    };
+    // This row's 8 scale bytes of the chunk in slot `slot` (group g uses bytes 2g, 2g + 1 of
+    // its warp's half).
+    auto load_scales = [&](int slot) -> uint2 {
+      return *reinterpret_cast<const uint2*>(w_slot(p, slot) + kTileCodeBytes + row * kRowScaleBytes);
+    };
+    auto lut = [&](uint2 sfw, int g, uint32_t& s0, uint32_t& s1) {
+      const uint32_t sw = (hsel + (g >> 1)) ? sfw.y : sfw.x;
+      s0 = ctl.scale_lut[__byte_perm(sw, 0, 0x4440 + 2 * (g & 1))];
+      s1 = ctl.scale_lut[__byte_perm(sw, 0, 0x4441 + 2 * (g & 1))];
     };
     bool more = advance();
-    if (more) ok = fetch();
+    uint4 cg = make_uint4(0, 0, 0, 0);   // codes of the group about to be converted
+    uint2 sfw = make_uint2(0, 0);        // scale bytes of the current chunk
+    uint32_t s0 = 0, s1 = 0;             // its two scale-table entries
+    if (more) {
+      ok = ptx::mbar_wait_sleep(&pc.w_full[st.slot], st.phase);
+      if (ok) {
+        sfw = load_scales(st.slot);
+        cg = load_codes(st.slot, 0);
+        lut(sfw, 0, s0, s1);
+      }
+    }
     while (ok && more) {
+#ifdef MUSE_TRACE
+      if (q == 0 && hsel == 0 && lane == 0) MUSE_TRACE_SEQ(trace::kTrF, p, tr_c);
+#endif
       const int ab = ar.slot;
-      // 16 columns (32 elements) at a time: column 16 * c4 + 4 * word + pair of this lane
+      const int cur = st.slot;
+      bool next_loaded = false, more_next = false;
+      uint2 sfw_next = sfw;
 #pragma unroll
-      for (int c = 0; c < 2 * kHalves; ++c) {
+      for (int g = 0; g < kGroups; ++g) {
+        // issue the next group's reads before converting this one
+        uint4 cn = cg;
+        uint32_t n0 = s0, n1 = s1;
+        if (g + 1 < kGroups) {
+          cn = load_codes(cur, g + 1);
+          lut(sfw, g + 1, n0, n1);
+        } else {
+          // every byte of this chunk is read: hand the slot back, then look ahead
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(&pc.w_empty[cur]);
+          st.next(Sw);
+          more_next = advance();
+          if (more_next && __all_sync(0xffffffffu, ptx::mbar_try_wait(&pc.w_full[st.slot], st.phase))) {
+            sfw_next = load_scales(st.slot);
+            cn = load_codes(st.slot, 0);
+            next_loaded = true;
+          }
+        }
         uint32_t out[16];
-        const uint4 c4 = cw[c];
-        dequant8(c4.x, sc[2 * c], m16, m64, &out[0]);
-        dequant8(c4.y, sc[2 * c], m16, m64, &out[4]);
-        dequant8(c4.z, sc[2 * c + 1], m16, m64, &out[8]);
-        dequant8(c4.w, sc[2 * c + 1], m16, m64, &out[12]);
-        if (c == 0 && !ptx::mbar_wait_sleep(&pc.a_empty[ab], ar.phase ^ 1)) {
+        dequant8(cg.x, s0, m16, m64, &out[0]);
+        dequant8(cg.y, s0, m16, m64, &out[4]);
+        dequant8(cg.z, s1, m16, m64, &out[8]);
+        dequant8(cg.w, s1, m16, m64, &out[12]);
+        if (g == 0 && !ptx::mbar_wait_sleep(&pc.a_empty[ab], ar.phase ^ 1)) {
           ok = false;
           break;
         }
-        ptx::tmem_st16(lane_col0 + ab * kACols + hsel * 32 + c * 16, out);
+        ptx::tmem_st16(lane_col0 + ab * kACols + hsel * 32 + g * 16, out);
+        cg = cn;
+        s0 = n0;
+        s1 = n1;
       }
       if (!ok) break;
       ptx::tmem_wait_st();
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(&pc.a_full[ab]);
+#ifdef MUSE_TRACE
+      if (q == 0 && hsel == 0 && lane == 0) MUSE_TRACE_SEQ(trace::kTrA, p, tr_c);
+      ++tr_c;
+#endif
       ar.next(geo.n_a);
-      // the next chunk's bytes: read after the hand-off, so the MMA of this chunk never waits
-      // for the next weight tile to land
-      more = advance();
-      if (more) ok = fetch();
+      more = more_next;
+      if (!more) break;
+      if (!next_loaded) {   // the next tile had not landed during the last group: wait for it now
+        if (!ptx::mbar_wait_sleep(&pc.w_full[st.slot], st.phase)) {
+          ok = false;
+          break;
+        }
+        sfw_next = load_scales(st.slot);
+        cg = load_codes(st.slot, 0);
+      }
+      sfw = sfw_next;
+      lut(sfw, 0, s0, s1);
     }
     if (!ok && lane == 0) record_error(a.error_flag, 4);
   }
@@ -778,8 +918,10 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
+  if (threadIdx.x == 0) MUSE_TRACE_AT(3);
   if (warp == kMmaWarp0) ptx::tmem_dealloc(tbase, kTmemCols);
-  if (kFused && a.fused) combine_tokens(ctl, a, n_local, n_box);
+  if (kFused && a.fused) combine_tokens(ctl, a, n_local);
+  if (threadIdx.x == 0) MUSE_TRACE_AT(4);
 }
 
 // Host-side view of one instantiation.
@@ -812,29 +954,32 @@ int read_device_status(int* status, int reset) {
 }
 
 // Pipelines per CTA for a token tile: three issuers fit the tensor memory only with N = 16.
-int pick_pipes(int n_box) { return n_box <= 16 ? kDecodePipes : 2; }
+int pick_pipes(int n_box, bool pair) { return pair ? 1 : n_box <= 16 ? kDecodePipes : 2; }
 // Dequant warps per pipeline for a token tile.
-int pick_dw(int n_box) { return n_box <= 16 ? kDecodeDW : 4; }
+int pick_dw(int n_box, bool pair) { return pair ? 8 : n_box <= 16 ? kDecodeDW : 4; }
 
-int pipe_cols(int pipes) { return pipes == 3 ? Variant<3, 4>::kPipeCols : Variant<2, 4>::kPipeCols; }
+int pipe_cols(int pipes) {
+  return pipes == 1 ? Variant<1, 8>::kPipeCols : pipes == 3 ? Variant<3, 4>::kPipeCols : Variant<2, 4>::kPipeCols;
+}
 static_assert(kDecodePipes == 2 || kDecodePipes == 3, "decode pipelines");
 
-size_t gemm_smem_bytes(int n_box, int w_stages, int b_stages) {
-  const Geo g = make_geo(pipe_cols(pick_pipes(n_box)), n_box, w_stages, b_stages);
-  return 1024 + (size_t)pick_pipes(n_box) * g.pipe_bytes + sizeof(SharedCtl);
+size_t gemm_smem_bytes(int n_box, bool pair, int w_stages, int b_stages) {
+  const Geo g = make_geo(pipe_cols(pick_pipes(n_box, pair)), n_box, w_stages, b_stages, pair);
+  return 1024 + (size_t)pick_pipes(n_box, pair) * g.pipe_bytes + sizeof(SharedCtl);
 }
 
 // Ring depths for a token tile: the deepest weight ring that fits 226 KB with one activation
 // slot more than weight slots (an activation slot lives until its MMAs complete, a weight slot
-// only until it has been read), else equal depths.
-int pick_stages(int n_box, int* b_stages) {
-  const int P = pick_pipes(n_box);
-  const Geo g = make_geo(pipe_cols(P), n_box, 1, 1);
+// only until it has been read), else equal depths; pair items (64 KiB activation slots) take
+// two activation slots and the deepest weight ring beside them.
+int pick_stages(int n_box, bool pair, int* b_stages) {
+  const int P = pick_pipes(n_box, pair);
+  const Geo g = make_geo(pipe_cols(P), n_box, 1, 1, pair);
   const size_t budget = (226u * 1024u - sizeof(SharedCtl) - 1024) / P;
   for (int sw = kMaxStages; sw >= 2; --sw) {
-    for (int extra = 1; extra >= 0; --extra) {
+    for (int extra = 1; extra >= (pair ? 2 - sw : 0); --extra) {
       const int sb = sw + extra;
-      if (sb <= kMaxStages && sw * (size_t)kWStageBytes + sb * (size_t)g.b_bytes <= budget) {
+      if (sb >= 2 && sb <= kMaxStages && sw * (size_t)kWStageBytes + sb * (size_t)g.b_bytes <= budget) {
         *b_stages = sb;
         return sw;
       }
@@ -844,7 +989,7 @@ int pick_stages(int n_box, int* b_stages) {
   return 2;
 }
 
-template <int P, int DW, bool kFused>
+template <int P, int DW, bool kFused, bool kPair = false>
 cudaError_t launch_variant(int grid, size_t smem, bool cooperative, const CUtensorMap& tmap_b,
                            const CUtensorMap& tmap_x, const CUtensorMap& tmap_b2, const GemmArgs& args,
                            cudaStream_t stream) {
@@ -858,7 +1003,7 @@ cudaError_t launch_variant(int grid, size_t smem, bool cooperative, const CUtens
   attr[0].val.cooperative = cooperative ? 1 : 0;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, expert_gemm_tc<P, DW, kFused>, tmap_b, tmap_x, tmap_b2, args);
+  return cudaLaunchKernelEx(&cfg, expert_gemm_tc<P, DW, kFused, kPair>, tmap_b, tmap_x, tmap_b2, args);
 }
 
 int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, const CUtensorMap& tmap_b2,
@@ -872,10 +1017,12 @@ int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, con
     if (e != cudaSuccess) return e;
   }
   if (!g_attr_set[dev]) {
-    const void* fns[4] = {(const void*)expert_gemm_tc<2, 4, false>, (const void*)expert_gemm_tc<2, 4, true>,
-                          (const void*)expert_gemm_tc<kDecodePipes, kDecodeDW, false>,
-                          (const void*)expert_gemm_tc<kDecodePipes, kDecodeDW, true>};
-    for (int i = 0; i < 4 && e == cudaSuccess; ++i)
+    const void* fns[5] = {(const void*)expert_gemm_tc<2, 4, false, false>,
+                          (const void*)expert_gemm_tc<2, 4, true, false>,
+                          (const void*)expert_gemm_tc<kDecodePipes, kDecodeDW, false, false>,
+                          (const void*)expert_gemm_tc<kDecodePipes, kDecodeDW, true, false>,
+                          (const void*)expert_gemm_tc<1, 8, false, true>};
+    for (int i = 0; i < 5 && e == cudaSuccess; ++i)
       e = cudaFuncSetAttribute(fns[i], cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
     if (e != cudaSuccess) return e;
     g_attr_set[dev] = true;
@@ -884,7 +1031,9 @@ int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, con
     return MUSE_ERR_UNSUPPORTED_SHAPE;
   if (args.n_phases < 1 || args.n_phases > 2 || (args.fused && args.n_phases != 2))
     return MUSE_ERR_INVALID_ARGUMENT;
-  const Geo g = make_geo(pipe_cols(pick_pipes(args.n_box)), args.n_box, args.stages, args.b_stages);
+  const bool pair = args.pair_tiles != 0;
+  if (pair && (args.fused || args.route_inline || args.n_box != 128)) return MUSE_ERR_INVALID_ARGUMENT;
+  const Geo g = make_geo(pipe_cols(pick_pipes(args.n_box, pair)), args.n_box, args.stages, args.b_stages, pair);
   if (g.n_a < 2) return MUSE_ERR_UNSUPPORTED_SHAPE;
   if (args.route_inline &&
       (args.n_pairs > kMaxInlinePairs || args.n_box > kMaxInlineBox || !args.ids || !args.pair_order ||
@@ -894,15 +1043,25 @@ int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, con
   if (args.fused && (!args.route_inline || !args.ph[1].signal || !args.ph[1].wait_for || !args.out ||
                      !args.topk_weights || args.top_k > kMaxTopK || args.hidden % 128))
     return MUSE_ERR_INVALID_ARGUMENT;
-  const size_t smem = gemm_smem_bytes(args.n_box, args.stages, args.b_stages);
+  const size_t smem = gemm_smem_bytes(args.n_box, pair, args.stages, args.b_stages);
   if (smem > 227u * 1024u) return MUSE_ERR_UNSUPPORTED_SHAPE;
   const int grid = g_num_sms[dev];
+#ifdef MUSE_TRACE
+  if (trace::g_host_buf) {  // this launch's block of the attached stamp buffer
+    unsigned long long* p = trace::g_host_buf + (size_t)(trace::g_host_next++ % trace::g_host_slots) * grid *
+                                                    trace::kTraceStride;
+    e = cudaMemcpyToSymbolAsync(trace::g_trace_buf, &p, sizeof(p), 0, cudaMemcpyHostToDevice, stream);
+    if (e != cudaSuccess) return e;
+  }
+#endif
   // A fused launch waits across CTAs (GEMM2 items on GEMM1 tiles, the combine on GEMM2 tiles):
   // it is launched cooperatively, so either every CTA is resident at once or the launch fails.
   const bool decode = args.n_box <= 16;  // the decode variant: kDecodePipes x kDecodeDW
   if (args.fused)
     e = decode ? launch_variant<kDecodePipes, kDecodeDW, true>(grid, smem, true, tmap_b, tmap_x, tmap_b2, args, stream)
                : launch_variant<2, 4, true>(grid, smem, true, tmap_b, tmap_x, tmap_b2, args, stream);
+  else if (pair)
+    e = launch_variant<1, 8, false, true>(grid, smem, false, tmap_b, tmap_x, tmap_b2, args, stream);
   else
     e = decode ? launch_variant<kDecodePipes, kDecodeDW, false>(grid, smem, false, tmap_b, tmap_x, tmap_b2, args, stream)
                : launch_variant<2, 4, false>(grid, smem, false, tmap_b, tmap_x, tmap_b2, args, stream);
@@ -911,3 +1070,17 @@ int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, con
 }
 
 }  // namespace muse
+
+#ifdef MUSE_TRACE
+// Traced builds only: attach (or, with null, detach) a stamp buffer for the expert GEMM's next
+// `launches` launches on the current device, each gridDim.x * kTraceStride u64 values (launch
+// i writes block i; later launches wrap around).
+extern "C" int muse_moe_trace_attach(void* buf, int launches) {
+  muse::trace::g_host_buf = static_cast<unsigned long long*>(buf);
+  muse::trace::g_host_slots = launches > 0 ? launches : 1;
+  muse::trace::g_host_next = 0;
+  unsigned long long* p = nullptr;
+  return (int)cudaMemcpyToSymbol(muse::trace::g_trace_buf, &p, sizeof(p));
+}
+extern "C" int muse_moe_trace_stride(void) { return muse::trace::kTraceStride; }
+#endif

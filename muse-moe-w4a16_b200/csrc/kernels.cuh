@@ -50,7 +50,9 @@ struct PhaseArgs {
                            // the kernel also splits any phase with fewer than 4 items per CTA)
   int b_source;            // B operand: 0 tmap_b boxes at the tile's rows (expert-grouped rows),
                            // 1 four-row gathers of x by token (tmap_x), 2 tmap_b2 boxes
-  int* signal;             // per-token-tile counters: each epilogue warp adds 1 per item (or null)
+  int* signal;             // single launch: GEMM1 -- per-token-tile counters, each epilogue warp
+                           // adds 1 per item of the tile; GEMM2 -- one completion counter, each
+                           // epilogue warp adds 1 after its last item (else null)
   const int* wait_for;     // counters that must reach wait_target before B is loaded (or null)
   int wait_target;
 };
@@ -61,6 +63,7 @@ struct GemmArgs {
   int32_t* offsets;        // [n_local + 1] expert ranges of the pair rows (written if route_inline)
   int n_local;
   int n_box;               // token tile = MMA N (16, 32, 64 or 128)
+  int pair_tiles;          // items cover two token tiles (one pipeline; n_box 128, separate launches)
   int stages;              // weight-tile ring depth (shared memory)
   int b_stages;            // activation-box ring depth (shared memory)
   int n_phases;            // 1 or 2
@@ -79,9 +82,8 @@ struct GemmArgs {
   int32_t* pair_order;
   int32_t* pair_row;
   // fused: after the GEMMs, each CTA combines tokens blockIdx.x, blockIdx.x + G, ... once the
-  // counters ph[1].signal of their tiles reach combine_target.
+  // GEMM2 completion counter ph[1].signal has every epilogue warp's increment (4 per CTA).
   int fused;
-  int combine_target;
   int tokens, hidden;
   const float* topk_weights;
   void* out;
@@ -99,9 +101,10 @@ int launch_route(const int32_t* ids, int tokens, int top_k, int local_start, int
 int launch_gather(const uint16_t* x, const int32_t* offsets, const int32_t* pair_order, int n_local,
                   int top_k, int max_rows, int hidden, uint16_t* xs, cudaStream_t stream);
 
-size_t gemm_smem_bytes(int n_box, int w_stages, int b_stages);
-// Weight-ring depth for a token tile; *b_stages receives the activation-ring depth.
-int pick_stages(int n_box, int* b_stages);
+size_t gemm_smem_bytes(int n_box, bool pair, int w_stages, int b_stages);
+// Weight-ring depth for a token tile (pair: items of two token tiles); *b_stages receives the
+// activation-ring depth.
+int pick_stages(int n_box, bool pair, int* b_stages);
 // tmap_b / tmap_b2: bf16 row buffers read as n_box-row boxes; tmap_x: x read by four-row gathers.
 // A fused launch is cooperative (all CTAs resident) and needs its counters zeroed beforehand.
 int launch_expert_gemm(const CUtensorMap& tmap_b, const CUtensorMap& tmap_x, const CUtensorMap& tmap_b2,

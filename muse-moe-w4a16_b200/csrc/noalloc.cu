@@ -16,8 +16,11 @@
 //     streams, or two host threads) race on it and must be serialised by the caller;
 //   * the array keeps whatever the last call left in it. No part of it has to start at zero:
 //     every value the layer reads from its scratch was written earlier in the same call;
-//   * the first call on a device looks up the array's device address (with that device
-//     current) and caches it; make that first call before any stream capture.
+//   * every call looks the array's device address up on the current device (cheap once the
+//     library's module is loaded), so a device reset or a re-created primary context, which
+//     may move the array, is followed; a call made while its stream is being captured cannot
+//     do the lookup and uses the address of the last call on that device -- make one call on
+//     the device before capturing, and capture again after a device reset.
 #include <mutex>
 
 #include "common.cuh"
@@ -35,19 +38,25 @@ static __device__ __align__(256) unsigned char g_static_scratch[kStaticScratchBy
 std::mutex g_setup_mutex;
 void* g_scratch_addr[kMaxDevices] = {nullptr};
 
-// Device address of g_static_scratch on the current device, looked up once per device.
-int static_scratch(void** addr) {
+// Device address of g_static_scratch on the current device: looked up on every call, and
+// remembered per device for calls made while `stream` is being captured.
+int static_scratch(cudaStream_t stream, void** addr) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= kMaxDevices) return MUSE_ERR_NO_DEVICE;
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  e = cudaStreamIsCapturing(stream, &cap);
+  if (e != cudaSuccess) return e;
   std::lock_guard<std::mutex> lock(g_setup_mutex);
-  if (!g_scratch_addr[dev]) {
+  if (cap == cudaStreamCaptureStatusNone) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_static_scratch);
     if (e != cudaSuccess) return e;
     if (!p) return MUSE_ERR_NO_DEVICE;
     g_scratch_addr[dev] = p;
+  } else if (!g_scratch_addr[dev]) {
+    return MUSE_ERR_INVALID_ARGUMENT;   // first call on this device inside a capture
   }
   *addr = g_scratch_addr[dev];
   return MUSE_OK;
@@ -68,7 +77,7 @@ extern "C" int muse_moe_forward_noalloc(const void* x, const int32_t* topk_ids,
   if (rc) return rc;
   if (need > muse::kStaticScratchBytes) return MUSE_ERR_SCRATCH_LIMIT;
   void* scratch = nullptr;
-  if ((rc = muse::static_scratch(&scratch))) return rc;
+  if ((rc = muse::static_scratch((cudaStream_t)stream, &scratch))) return rc;
   return muse_moe_forward(x, topk_ids, topk_weights, tokens, top_k, local_start, local_count,
                           hidden, inter, w13p, w13_sfp, w13_gs, w2p, w2_sfp, w2_gs, post_norm_w,
                           out, scratch, muse::kStaticScratchBytes, stream);

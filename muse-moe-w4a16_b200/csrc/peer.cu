@@ -4,20 +4,34 @@
 // prefill layout) -- done by this kernel instead of a collective library.
 //
 // Each rank's share lives in its own symmetric buffer; the buffers of all ranks are mapped
-// into every rank's address space (peer pointers). Every rank keeps, in its own flag array,
-// 8 peer slots, its generation counter (slot 8: calls completed) and a finished-block count
-// (slot 9). A call with generation g = counter + 1 (the same on every rank):
-//   1. block 0 publishes "my share of call g is complete" by writing g into slot `rank` of
-//      every rank's flag array (system-scope release after a system fence, so the share's
+// into every rank's address space (peer pointers). Every rank keeps, in its own flag array
+// (kFlagWords uint32, zero before the first call), one round-1 and one round-2 slot per peer,
+// its generation counter (calls completed) and three bookkeeping words. A call with generation
+// g = counter + 1 (the same on every rank):
+//   1. block 0 publishes "my share of call g is complete" by writing g into round-1 slot `rank`
+//      of every rank's flag array (system-scope release after a system fence, so the share's
 //      bytes -- written by the previous kernel on this stream -- are visible first);
-//   2. every block waits (acquire, bounded) until all R peer slots of its own array hold g;
-//   3. out[i] = bf16(sum over r = 0 .. R-1 of share_r[offset + i]) from the share buffers of
-//      parity g & 1, in the same order on every rank, so all ranks produce identical bits;
-//   4. the last block to finish stores g as the new counter.
+//   2. every block waits (acquire, bounded) until all round-1 slots of its own array hold g;
+//   3. reduce: element i of this rank's slice = bf16(sum over r = 0 .. R-1, in that order, of
+//      share_r[i]) from the share buffers of parity g & 1. The slice is the whole share (one-round
+//      all-reduce), this rank's 1/R of it (reduce-scatter), or, for the two-round all-reduce,
+//      this rank's 1/R written both to the output and to its bf16 staging buffer;
+//   4. two-round all-reduce only: the last block of this rank to finish step 3 publishes round 2
+//      to every rank; every block waits (bounded) for all round-2 slots and then copies every
+//      other rank's slice from that rank's staging buffer (gather);
+//   5. the last block to finish stores g as the new counter -- unless a wait expired.
+// Every element is summed by exactly one rank in rank order, so all ranks hold identical bits.
 // The generation lives on the device, so a captured graph of the call stays valid across
 // replays. Callers write call g's share into buffer g & 1: a rank rewrites a buffer only two
 // calls later, after every peer has signalled the call in between (which it does only after
-// finishing its reads of this rank's older share).
+// finishing its reads of this rank's older share). A staging buffer is rewritten by its owner
+// in the next call, after every peer's round-1 signal of that call, i.e. after their gathers.
+//
+// Failure: a wait that runs past the caller's limit sets the sticky device status to 6 and
+// this rank's call stops without advancing its generation (the output is then unspecified); a
+// call whose generation parity differs from the caller's expectation does nothing and sets 7.
+// Either way the exchange is out of step: re-create its flag arrays (zeroed, then a barrier of
+// all ranks) before the next call.
 #include "common.cuh"
 #include "kernels.cuh"
 #include "ptx.cuh"
@@ -26,15 +40,24 @@ namespace muse {
 namespace {
 
 constexpr int kMaxPeers = 8;
-constexpr int kGenSlot = 8, kDoneSlot = 9;
+constexpr int kRound2 = 8;          // slots [8, 16): round-2 signals
+constexpr int kGenSlot = 16;        // calls completed
+constexpr int kDoneA = 17;          // blocks past step 3 (two-round) in the current call
+constexpr int kDoneB = 18;          // blocks finished in the current call
+constexpr int kFail = 19;           // a wait of the current call expired
+constexpr unsigned long long kDefaultTimeoutNs = 1000000000ull;  // 1 s
+
+enum Mode { kAllReduce1 = 0, kReduceScatter = 1, kAllReduce2 = 2 };
 
 struct PeerArgs {
   const float* share[2][kMaxPeers];  // share buffers of parity 0 / 1 of rank r (peer pointers)
   uint32_t* flags[kMaxPeers];        // flag array of rank r
-  int ranks, rank;
-  size_t n4;                         // elements / 4
-  size_t offset4;                    // first element / 4 (0, or this rank's slice)
-  uint16_t* out;                     // bf16 [n], this rank's memory
+  uint16_t* staging[kMaxPeers];      // bf16 staging buffer of rank r (two-round all-reduce)
+  int ranks, rank, mode, expect_parity;
+  unsigned long long timeout_ns;
+  size_t slice4;                     // elements of one rank's slice / 4
+  size_t n4;                         // elements of a share / 4
+  uint16_t* out;                     // bf16, this rank's memory
   int* error_flag;
 };
 
@@ -48,62 +71,125 @@ __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
-__global__ void __launch_bounds__(256) peer_allreduce_kernel(const PeerArgs a) {
+__device__ __forceinline__ unsigned long long global_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait (one thread) until slots [base, base + ranks) of `mine` hold at least gen. Gives up after
+// timeout_ns, or as soon as another block of this rank has recorded a failure.
+__device__ bool wait_slots(const uint32_t* mine, int base, int ranks, uint32_t gen,
+                           unsigned long long timeout_ns) {
+  const unsigned long long t0 = global_ns();
+  for (int r = 0; r < ranks; ++r) {
+    unsigned ns = 32;
+    while (ld_acquire_sys(mine + base + r) < gen) {
+      if (global_ns() - t0 > timeout_ns) return false;
+      if (*reinterpret_cast<const volatile uint32_t*>(mine + kFail)) return false;
+      __nanosleep(ns);
+      if (ns < 256) ns <<= 1;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ uint2 sum_bf16x4(const PeerArgs& a, int par, size_t i4) {
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int r = 0; r < a.ranks; ++r) {
+    const float4 v = __ldcv(reinterpret_cast<const float4*>(a.share[par][r]) + i4);
+    acc.x += v.x;
+    acc.y += v.y;
+    acc.z += v.z;
+    acc.w += v.w;
+  }
+  __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
+  __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
+  uint2 packed;
+  packed.x = *reinterpret_cast<uint32_t*>(&lo);
+  packed.y = *reinterpret_cast<uint32_t*>(&hi);
+  return packed;
+}
+
+__global__ void __launch_bounds__(256) peer_exchange_kernel(const PeerArgs a) {
   __shared__ int s_ok;
   __shared__ uint32_t s_gen;
   uint32_t* mine = a.flags[a.rank];
   if (threadIdx.x == 0) s_gen = *reinterpret_cast<volatile uint32_t*>(mine + kGenSlot) + 1u;
   __syncthreads();
   const uint32_t gen = s_gen;
+  if (a.expect_parity >= 0 && (int)(gen & 1u) != a.expect_parity) {
+    // the caller's share went to the other buffer: touch nothing, say so
+    if (blockIdx.x == 0 && threadIdx.x == 0) atomicExch(a.error_flag, 7);
+    return;
+  }
   if (blockIdx.x == 0 && threadIdx.x < a.ranks) {
     __threadfence_system();
     st_release_sys(a.flags[threadIdx.x] + a.rank, gen);
   }
   if (threadIdx.x == 0) {
-    bool ok = true;
-    const long long t0 = clock64();
-    for (int r = 0; r < a.ranks && ok; ++r) {
-      unsigned ns = 32;
-      while (ld_acquire_sys(mine + r) < gen) {
-        if (clock64() - t0 > ptx::kWaitCycles) {
-          ok = false;
-          break;
-        }
-        __nanosleep(ns);
-        if (ns < 256) ns <<= 1;
-      }
+    s_ok = wait_slots(mine, 0, a.ranks, gen, a.timeout_ns);
+    if (!s_ok) {
+      atomicExch(mine + kFail, 1u);
+      atomicExch(a.error_flag, 6);
     }
-    if (!ok) atomicExch(a.error_flag, 6);
-    s_ok = ok;
   }
   __syncthreads();
-  if (s_ok) {  // else a peer never signalled: the output is left alone, the status says why
-    const int par = gen & 1u;
-    for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < a.n4; i += (size_t)gridDim.x * blockDim.x) {
-      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-      for (int r = 0; r < a.ranks; ++r) {
-        const float4 v = __ldcv(reinterpret_cast<const float4*>(a.share[par][r]) + a.offset4 + i);
-        acc.x += v.x;
-        acc.y += v.y;
-        acc.z += v.z;
-        acc.w += v.w;
-      }
-      __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
-      __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
-      uint2 packed;
-      packed.x = *reinterpret_cast<uint32_t*>(&lo);
-      packed.y = *reinterpret_cast<uint32_t*>(&hi);
-      reinterpret_cast<uint2*>(a.out)[i] = packed;
+  const int par = gen & 1u;
+  const size_t stride = (size_t)gridDim.x * blockDim.x;
+  const size_t tid = blockIdx.x * (size_t)blockDim.x + threadIdx.x;
+  if (s_ok) {
+    // step 3: this rank's slice (all of it for the one-round all-reduce)
+    const size_t lo = a.mode == kAllReduce1 ? 0 : (size_t)a.rank * a.slice4;
+    const size_t hi = a.mode == kAllReduce1 ? a.n4 : min(lo + a.slice4, a.n4);
+    uint2* out = reinterpret_cast<uint2*>(a.out);
+    uint2* stage = a.mode == kAllReduce2 ? reinterpret_cast<uint2*>(a.staging[a.rank]) : nullptr;
+    for (size_t i = lo + tid; i < hi; i += stride) {
+      const uint2 v = sum_bf16x4(a, par, i);
+      out[a.mode == kReduceScatter ? i - lo : i] = v;
+      if (stage) stage[i] = v;
     }
   }
-  // the last block out advances the generation (every block has read it by now)
+  if (a.mode == kAllReduce2) {
+    // step 4: once every block of this rank has written its part of the slice, tell the peers
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      if (atomicAdd(mine + kDoneA, 1u) == gridDim.x - 1) {
+        mine[kDoneA] = 0;
+        if (!*reinterpret_cast<volatile uint32_t*>(mine + kFail))
+          for (int r = 0; r < a.ranks; ++r) st_release_sys(a.flags[r] + kRound2 + a.rank, gen);
+      }
+      if (s_ok) {
+        s_ok = wait_slots(mine, kRound2, a.ranks, gen, a.timeout_ns);
+        if (!s_ok) {
+          atomicExch(mine + kFail, 1u);
+          atomicExch(a.error_flag, 6);
+        }
+      }
+    }
+    __syncthreads();
+    if (s_ok) {
+      uint4* out = reinterpret_cast<uint4*>(a.out);
+      const size_t slice8 = a.slice4 / 2, n8 = a.n4 / 2;
+      for (int k = 1; k < a.ranks; ++k) {
+        const int r = (a.rank + k) % a.ranks;   // start with a different peer on every rank
+        const size_t lo = (size_t)r * slice8, hi = min(lo + slice8, n8);
+        const uint4* src = reinterpret_cast<const uint4*>(a.staging[r]);
+        for (size_t i = lo + tid; i < hi; i += stride) out[i] = __ldcv(src + i);
+      }
+    }
+  }
+  // step 5: the last block out advances the generation (every block has read it by now)
   __syncthreads();
   if (threadIdx.x == 0) {
     __threadfence();
-    if (atomicAdd(mine + kDoneSlot, 1u) == gridDim.x - 1) {
-      mine[kDoneSlot] = 0;
+    if (atomicAdd(mine + kDoneB, 1u) == gridDim.x - 1) {
+      mine[kDoneB] = 0;
+      const bool failed = *reinterpret_cast<volatile uint32_t*>(mine + kFail) != 0;
+      mine[kFail] = 0;
       __threadfence();
-      *reinterpret_cast<volatile uint32_t*>(mine + kGenSlot) = gen;
+      if (!failed) *reinterpret_cast<volatile uint32_t*>(mine + kGenSlot) = gen;
     }
   }
 }
@@ -114,11 +200,13 @@ __global__ void __launch_bounds__(256) peer_allreduce_kernel(const PeerArgs a) {
 namespace muse {
 namespace {
 
-int launch_peer_sum(const uint64_t* shares0, const uint64_t* shares1, const uint64_t* flags, int ranks,
-                    int rank, size_t offset, size_t n, void* out, cudaStream_t stream) {
+int launch_peer(const uint64_t* shares0, const uint64_t* shares1, const uint64_t* flags,
+                const uint64_t* staging, int ranks, int rank, size_t n, int mode, int expect_parity,
+                long long timeout_us, void* out, cudaStream_t stream) {
   if (!shares0 || !shares1 || !flags || !out || ranks < 1 || ranks > kMaxPeers || rank < 0 ||
-      rank >= ranks || n % 8 || offset % 8)
+      rank >= ranks || n % 8 || expect_parity < -1 || expect_parity > 1 || timeout_us < 0)
     return MUSE_ERR_INVALID_ARGUMENT;
+  if (mode == kAllReduce2 && !staging) return MUSE_ERR_INVALID_ARGUMENT;
   PeerArgs a{};
   for (int r = 0; r < ranks; ++r) {
     if (!shares0[r] || !shares1[r] || !flags[r] || shares0[r] % 16 || shares1[r] % 16 || flags[r] % 4)
@@ -126,34 +214,68 @@ int launch_peer_sum(const uint64_t* shares0, const uint64_t* shares1, const uint
     a.share[0][r] = reinterpret_cast<const float*>(shares0[r]);
     a.share[1][r] = reinterpret_cast<const float*>(shares1[r]);
     a.flags[r] = reinterpret_cast<uint32_t*>(flags[r]);
+    if (mode == kAllReduce2) {
+      if (!staging[r] || staging[r] % 16) return MUSE_ERR_INVALID_ARGUMENT;
+      a.staging[r] = reinterpret_cast<uint16_t*>(staging[r]);
+    }
   }
   if (reinterpret_cast<uintptr_t>(out) % 16) return MUSE_ERR_INVALID_ARGUMENT;
   a.ranks = ranks;
   a.rank = rank;
+  a.mode = mode;
+  a.expect_parity = expect_parity;
+  a.timeout_ns = timeout_us ? (unsigned long long)timeout_us * 1000ull : kDefaultTimeoutNs;
   a.n4 = n / 4;
-  a.offset4 = offset / 4;
+  // a rank's slice: n / ranks rounded up to 8 elements (16-byte pieces of bf16)
+  const size_t slice = mode == kAllReduce1 ? n : (n / ranks + 7) / 8 * 8;
+  if (mode == kReduceScatter && slice * ranks != n) return MUSE_ERR_INVALID_ARGUMENT;
+  a.slice4 = slice / 4;
   a.out = static_cast<uint16_t*>(out);
   int rc = device_status_ptr(&a.error_flag);
   if (rc) return rc;
   // at least one block: an empty exchange (no tokens) still signals the peers and advances the
-  // generation, so every rank's count -- and the share buffer its caller writes next -- stays in step
-  const size_t blocks = a.n4 == 0 ? 1 : (a.n4 + 255) / 256;
-  peer_allreduce_kernel<<<blocks < 296 ? (unsigned)blocks : 296u, 256, 0, stream>>>(a);
+  // generation, so every rank's count -- and the share buffer its caller writes next -- stays in
+  // step. The two-round all-reduce waits across its own blocks (step 4), so it is launched
+  // cooperatively: all of its blocks are resident at once, or the launch fails.
+  const size_t work4 = mode == kAllReduce1 ? a.n4 : a.slice4;
+  size_t blocks = work4 == 0 ? 1 : (work4 + 255) / 256;
+  if (blocks > 296) blocks = 296;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)blocks);
+  cfg.blockDim = dim3(256);
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;
+  attr[0].val.cooperative = mode == kAllReduce2 ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, peer_exchange_kernel, a);
+  if (e != cudaSuccess) return e;
   return last_launch_status();
 }
 
 }  // namespace
 }  // namespace muse
 
+extern "C" int muse_moe_peer_exchange_bf16(const uint64_t* shares0, const uint64_t* shares1,
+                                           const uint64_t* flags, const uint64_t* staging, int ranks,
+                                           int rank, size_t n, int mode, int expect_parity,
+                                           long long timeout_us, void* out, muse_stream_t stream) {
+  if (mode < 0 || mode > 2) return MUSE_ERR_INVALID_ARGUMENT;
+  return muse::launch_peer(shares0, shares1, flags, staging, ranks, rank, n, mode, expect_parity,
+                           timeout_us, out, (cudaStream_t)stream);
+}
+
 extern "C" int muse_moe_peer_allreduce_bf16(const uint64_t* shares0, const uint64_t* shares1,
                                             const uint64_t* flags, int ranks, int rank, size_t n,
                                             void* out, muse_stream_t stream) {
-  return muse::launch_peer_sum(shares0, shares1, flags, ranks, rank, 0, n, out, (cudaStream_t)stream);
+  return muse::launch_peer(shares0, shares1, flags, nullptr, ranks, rank, n, muse::kAllReduce1, -1, 0,
+                           out, (cudaStream_t)stream);
 }
 
 extern "C" int muse_moe_peer_reduce_scatter_bf16(const uint64_t* shares0, const uint64_t* shares1,
                                                  const uint64_t* flags, int ranks, int rank,
                                                  size_t n_per_rank, void* out, muse_stream_t stream) {
-  return muse::launch_peer_sum(shares0, shares1, flags, ranks, rank, (size_t)rank * n_per_rank, n_per_rank,
-                               out, (cudaStream_t)stream);
+  return muse::launch_peer(shares0, shares1, flags, nullptr, ranks, rank, n_per_rank * ranks,
+                           muse::kReduceScatter, -1, 0, out, (cudaStream_t)stream);
 }

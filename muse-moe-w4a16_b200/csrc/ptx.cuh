@@ -227,6 +227,11 @@ __device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// Relaxed GPU-scope add; ordered after earlier stores only by a preceding fence.
+__device__ __forceinline__ void red_relaxed_gpu_add(int* p, int v) {
+  asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // Orders this thread's generic-proxy accesses of global memory with its async-proxy (TMA)
 // accesses: data written with plain stores by one CTA and read by another CTA's TMA.
 __device__ __forceinline__ void fence_proxy_async_global() {

@@ -11,15 +11,23 @@ addition per rank.
 Two layouts of the tokens:
   replicated (decode): every rank holds the same T tokens. Each rank writes its fp32 share
       [T, H] straight into its own symmetric buffer (mapped into every rank's address space),
-      and one kernel of this library (`muse_moe_peer_allreduce_bf16`) sums the R shares over
-      NVLink in rank order and casts to bf16 -- every rank returns the same bits. (With CPU
-      tensors, as in the gloo tests of the exchange logic, the shares are summed by an
-      all-reduce collective instead.)
+      and one kernel of this library (`muse_moe_peer_exchange_bf16`) sums the R shares over
+      NVLink in rank order and casts to bf16 -- every rank returns the same bits. Small shares
+      are summed whole by every rank (one round of flags); larger ones are reduce-scattered
+      (each rank sums its 1/R slice) and then all-gathered in bf16 from the ranks' staging
+      buffers (two rounds), so a rank reads ~1.5 x T x H x 4 bytes over NVLink instead of
+      R x T x H x 4. (With CPU tensors, as in the gloo tests of the exchange logic, the shares
+      are summed by an all-reduce collective instead.)
   sharded (prefill): rank r holds its own T_r tokens (T_r equal on every rank). Inputs are
       all-gathered (x bf16, ids, weights; NCCL), every rank writes its experts' share of all
-      R * T_r tokens into its symmetric buffer, and this library's peer kernel
-      (`muse_moe_peer_reduce_scatter_bf16`) returns each rank the rank-ordered sum for its own
-      tokens over NVLink. (CPU tensors: a reduce-scatter collective, as in the gloo tests.)
+      R * T_r tokens into its symmetric buffer, and this library's peer kernel (reduce-scatter
+      mode) returns each rank the rank-ordered sum for its own tokens over NVLink. (CPU tensors:
+      a reduce-scatter collective, as in the gloo tests.)
+
+Every exchange tells the kernel which share buffer (generation parity) the host wrote into; a
+disagreement with the device's count, or a peer that never signals within `timeout_us`, sets
+the library's device status (7 / 6) instead of summing the wrong buffers. `check_status()`
+reads it (synchronising) and raises; after such a failure call `reset_exchange()` on every rank.
 
 Collectives use fixed shapes (no counts sent to the host), so a call issues no host
 synchronisation.
@@ -85,10 +93,16 @@ class ExpertParallelMoE:
         self._local = local_fn
         self._cast = cast_fn or cast_bf16
         self._peer = None   # symmetric buffers of the decode exchange, set up on first use
-        self._gen = 0
+        self._gen = 0       # exchanges completed (the device keeps its own count; they agree)
+        self.timeout_us = 0  # bound of the exchange's waits for the peers (0: the library's 1 s)
+        # shares of at most this many bytes are summed whole by every rank (one flag round);
+        # larger ones are reduce-scattered and all-gathered (two rounds, ~R/1.5 x fewer bytes)
+        self.one_round_bytes = 1 << 20
 
-    def forward_replicated(self, data: Inputs) -> torch.Tensor:
-        """Decode layout: the same T tokens on every rank -> bf16 [T, H] on every rank."""
+    def forward_replicated(self, data: Inputs, stage_events: list | None = None) -> torch.Tensor:
+        """Decode layout: the same T tokens on every rank -> bf16 [T, H] on every rank.
+        `stage_events` (three torch.cuda.Event(enable_timing=True)), if given, are recorded before
+        this rank's layer kernels, between them and the exchange, and after the exchange."""
         x = data["hidden_states"]
         local = _with_local_range(data, self.experts)
         if x.shape[0] == 0:
@@ -99,21 +113,62 @@ class ExpertParallelMoE:
             dist.all_reduce(part, op=dist.ReduceOp.SUM, group=self.group)
             return self._cast(part)
         self._peer_buffers(x.shape[0] * x.shape[1], x.device)
-        self._gen += 1
-        return self._decode(local, self._gen & 1)
+        out = self._decode(local, (self._gen + 1) & 1, stage_events)
+        self._gen += 1      # only once both launches were accepted
+        return out
 
-    def _decode(self, local: Inputs, parity: int) -> torch.Tensor:
+    def exchange_mode(self, numel: int) -> int:
+        """Mode of muse_moe_peer_exchange_bf16 for a decode share of `numel` fp32 values."""
+        if self.world == 1 or numel * 4 * (self.world - 1) <= self.one_round_bytes:
+            return 0
+        return 2
+
+    def _decode(self, local: Inputs, parity: int, stage_events: list | None = None) -> torch.Tensor:
         """The rank's share written into its share buffer `parity`, then the peer exchange (the
-        kernel takes the generation, and so the parity it reads, from the device)."""
+        kernel takes the generation from the device and checks it has this parity)."""
         x = local["hidden_states"]
         T, H = x.shape
         peer = self._peer
         share = peer["buf"][parity * peer["cap"]:parity * peer["cap"] + T * H].view(T, H)
+        if stage_events:
+            stage_events[0].record()
         kernel_fn_partial(local, self.state, out=share)
+        if stage_events:
+            stage_events[1].record()
         out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
-        _lib.call("muse_moe_peer_allreduce_bf16", peer["shares"][0], peer["shares"][1], peer["flags"],
-                  self.world, self.rank, T * H, out.data_ptr(), torch.cuda.current_stream(x.device).cuda_stream)
+        self._exchange(T * H, self.exchange_mode(T * H), parity, out)
+        if stage_events:
+            stage_events[2].record()
         return out
+
+    def _exchange(self, n: int, mode: int, parity: int, out: torch.Tensor) -> None:
+        peer = self._peer
+        _lib.call("muse_moe_peer_exchange_bf16", peer["shares"][0], peer["shares"][1], peer["flags"],
+                  peer["staging"], self.world, self.rank, n, mode, parity, int(self.timeout_us),
+                  out.data_ptr(), torch.cuda.current_stream(out.device).cuda_stream)
+
+    def check_status(self) -> None:
+        """Raise MuseError if an exchange (or a layer kernel) on this device has failed since the
+        last check: 6 = a peer never signalled in time, 7 = generation parity mismatch. Reading
+        the status synchronises the device; it clears the status."""
+        st = _lib.device_status(reset=True)
+        if st:
+            raise _lib.MuseError(_lib.MUSE_ERR_DEVICE_TIMEOUT,
+                                 f"device status {st} on rank {self.rank}: the exchange is out of step; "
+                                 "call reset_exchange() on every rank")
+
+    def reset_exchange(self) -> None:
+        """Zero this rank's flags and generation count and wait for every rank to do the same
+        (collective): the exchange restarts from generation 1 on all ranks."""
+        if self._peer is None:
+            return
+        dev = self._peer["buf"].device
+        torch.cuda.synchronize(dev)
+        dist.barrier(group=self.group)
+        self._peer["buf"][self._peer["flags_at"]:].zero_()
+        torch.cuda.synchronize(dev)
+        self._gen = 0
+        dist.barrier(group=self.group)
 
     def decode_graphs(self, data: Inputs) -> "DecodeGraphs":
         """CUDA graphs of the decode call for these (device) inputs; see DecodeGraphs."""
@@ -136,16 +191,19 @@ class ExpertParallelMoE:
             torch.cuda.synchronize(device)
             dist.barrier(group=self.group)
         cap = (max(numel, 1 << 16) + 63) // 64 * 64        # floats; keeps the shares 256-byte aligned
-        buf = symm.empty(2 * cap + 64, dtype=torch.float32, device=device)
-        buf[2 * cap:].zero_()                                # flags and the generation counter start at 0
+        # [share 0: cap fp32 | share 1: cap fp32 | bf16 staging: cap bf16 | flags: 64 words]
+        flags_at = 2 * cap + cap // 2
+        buf = symm.empty(flags_at + 64, dtype=torch.float32, device=device)
+        buf[flags_at:].zero_()                               # flags and the generation counter start at 0
         torch.cuda.synchronize(device)
         handle = symm.rendezvous(buf, self.group if self.group is not None else dist.group.WORLD)
         bases = [int(p) for p in handle.buffer_ptrs]
         u64 = ctypes.c_uint64 * self.world
         self._peer = {
-            "buf": buf, "handle": handle, "cap": cap,
+            "buf": buf, "handle": handle, "cap": cap, "flags_at": flags_at,
             "shares": [u64(*[b + k * cap * 4 for b in bases]) for k in (0, 1)],
-            "flags": u64(*[b + 2 * cap * 4 for b in bases]),
+            "staging": u64(*[b + 2 * cap * 4 for b in bases]),
+            "flags": u64(*[b + flags_at * 4 for b in bases]),
         }
         self._gen = 0
         dist.barrier(group=self.group)                       # every rank's flags are zero before use
@@ -174,14 +232,14 @@ class ExpertParallelMoE:
             return self._cast(mine)
         H = x.shape[1]
         self._peer_buffers(R * t_r * H, x.device)
-        self._gen += 1
+        parity = (self._gen + 1) & 1
         peer = self._peer
-        base = (self._gen & 1) * peer["cap"]
+        base = parity * peer["cap"]
         share = peer["buf"][base:base + R * t_r * H].view(R * t_r, H)
         kernel_fn_partial(gathered, self.state, out=share)
         out = torch.empty((t_r, H), dtype=torch.bfloat16, device=x.device)
-        _lib.call("muse_moe_peer_reduce_scatter_bf16", peer["shares"][0], peer["shares"][1], peer["flags"],
-                  R, self.rank, t_r * H, out.data_ptr(), torch.cuda.current_stream(x.device).cuda_stream)
+        self._exchange(R * t_r * H, 1, parity, out)
+        self._gen += 1
         return out
 
 
@@ -208,7 +266,7 @@ class DecodeGraphs:
         if self.moe._peer is None or self.moe._peer["buf"] is not self.buf:
             raise _lib.MuseError(_lib.MUSE_ERR_INVALID_ARGUMENT,
                                  "the decode buffers were reallocated after this capture (reserve_decode first)")
-        self.moe._gen += 1
-        k = self.moe._gen & 1
+        k = (self.moe._gen + 1) & 1
         self.graphs[k].replay()
+        self.moe._gen += 1
         return self.outs[k]

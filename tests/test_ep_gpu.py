@@ -74,6 +74,20 @@ def _rank_main(rank, world, port, T, result_dir):
         assert torch.equal(again.view(torch.int16), shard.view(torch.int16))
         again = moe.forward_replicated(d)     # decode and prefill calls share the generation count
         assert torch.equal(again.view(torch.int16), rep.view(torch.int16))
+        # the two-round exchange (reduce-scatter, then all-gather of the bf16 slices) gives the
+        # same bits: every element is still summed once, in rank order
+        moe.one_round_bytes = 0
+        assert moe.exchange_mode(T * shape.hidden) == 2
+        for _ in range(2):
+            again = moe.forward_replicated(d)
+            assert torch.equal(again.view(torch.int16), rep.view(torch.int16))
+        graphs2 = moe.decode_graphs(d)
+        for _ in range(3):
+            got = graphs2.replay()
+            torch.cuda.synchronize()
+            assert torch.equal(got.view(torch.int16), rep.view(torch.int16))
+        moe.check_status()
+        del graphs, graphs2
         torch.cuda.synchronize()
         np.save(os.path.join(result_dir, f"rep{rank}.npy"), rep.view(torch.uint16).cpu().numpy())
         np.save(os.path.join(result_dir, f"shard{rank}.npy"), shard.view(torch.uint16).cpu().numpy())

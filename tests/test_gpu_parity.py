@@ -135,6 +135,20 @@ def test_layer_reference_problem_reduced(pkg, synth, bs, dist):
     assert err < 5e-3
 
 
+@pytest.mark.parametrize("T,K,E,lo,cnt", [(1024, 2, 6, 0, 4), (700, 4, 8, 2, 5), (1500, 3, 3, 0, 3)])
+def test_layer_pair_tile_items(pkg, synth, T, K, E, lo, cnt):
+    """Prefill-sized batches (>= 128 pairs per local expert on average) run items of two
+    128-token tiles that share each dequantised weight chunk; experts with an odd number of
+    tiles end with a one-tile item. Every row against the oracle."""
+    from muse_moe_w4a16_b200 import _lib
+    H, I = 256, 384
+    assert _lib.launch_plan(T, K, cnt, H, I)["pair_tiles"]
+    shape = synth.MoEShape(E, K, H, I, local_start=lo, local_count=cnt, router="zipf")
+    w = synth.baseline_weights(shape, seed=T + E)
+    err, _ = _check_layer(pkg, w, synth.baseline_input(shape, T, seed=T))
+    assert err < 5e-3
+
+
 def test_layer_tokens_without_local_pairs_are_zero(pkg, synth):
     shape = synth.MoEShape(16, 2, 256, 128, local_start=8, local_count=4, router="uniform")
     w = synth.baseline_weights(shape, seed=1)
