@@ -67,6 +67,8 @@ def parse_args(argv=None):
     ap.add_argument("--tokens", default=None, help="comma list overriding the workload's sweep")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-secondary", action="store_true", help="skip the secondary cfg2 block")
+    ap.add_argument("--experts", type=int, default=None,
+                    help="profiling size: the workload's shape with this many experts (all local)")
     return ap.parse_args(argv)
 
 
@@ -74,8 +76,9 @@ def peaks():
     if PEAKS_FILE.exists():
         p = json.loads(PEAKS_FILE.read_text())
         return {"hbm_gbs": float(p["hbm_gbs"]), "bf16_tflops": float(p["bf16_tflops"]),
+                "bf16_tflops_sustained": float(p.get("bf16_tflops_sustained", p["bf16_tflops"])),
                 "source": "measured"}
-    return dict(FALLBACK_PEAKS, source="fallback")
+    return dict(FALLBACK_PEAKS, bf16_tflops_sustained=1400.0, source="fallback")
 
 
 def geomean(v):
@@ -181,8 +184,11 @@ class ClockSampler:
 
 # ----------------------------------------------------------------------------- workloads
 
-def sweep(synth, name: str, tokens_arg: str | None):
+def sweep(synth, name: str, tokens_arg: str | None, experts: int | None = None):
     shape = synth.CONFIGS[name]
+    if experts:   # a profiling-sized copy of the workload: same H, I, K and router, fewer experts
+        import dataclasses
+        shape = dataclasses.replace(shape, n_experts=experts, local_start=0, local_count=None)
     tokens = tuple(int(t) for t in tokens_arg.split(",")) if tokens_arg else synth.TOKENS[name]
     return shape, tokens
 
@@ -255,7 +261,7 @@ def run_reference(args, world, rank):
 
     pkg = __graft_entry__.load_package()
     from muse_moe_w4a16_b200 import synth
-    shape, tokens = sweep(synth, args.workload, args.tokens)
+    shape, tokens = sweep(synth, args.workload, args.tokens, args.experts)
     cores = os.cpu_count() or 1
     w_np = numpy_weights(make_weights(synth, shape, "cuda" if torch.cuda.is_available() else "cpu"))
     del pkg
@@ -376,7 +382,7 @@ class Bench:
         pass, the CPU baseline and the parity check (the headline workload)."""
         args, world, dev, synth, traffic, _lib, pkg = (self.args, self.world, self.dev, self.synth,
                                                       self.traffic, self._lib, self.pkg)
-        shape = synth.CONFIGS[name]
+        shape = sweep(synth, name, None, self.args.experts if name == self.args.workload else None)[0]
         w = make_weights(synth, shape, dev)
         moe = None
         if world > 1:
@@ -475,10 +481,10 @@ class Bench:
         for t in tokens:
             got = graphs[t].replay()
             torch.cuda.synchronize()
-            mine = got.view(torch.int16).clone()
-            ref0 = mine.clone()
+            ref0 = got.clone()                       # bf16 (a byte copy through NCCL)
             torch.distributed.broadcast(ref0, 0)
-            equal = torch.tensor([1 if torch.equal(mine, ref0) else 0], device=self.dev)
+            same = torch.equal(got.view(torch.int16), ref0.view(torch.int16))
+            equal = torch.tensor([1 if same else 0], dtype=torch.int32, device=self.dev)
             torch.distributed.all_reduce(equal, op=torch.distributed.ReduceOp.MIN)
             row = {"ranks_bit_equal": bool(equal.item())}
             if rank == 0:
@@ -611,11 +617,12 @@ class Bench:
         dims = (shape.local_start, shape.n_local, shape.hidden, shape.inter)
         stage_us = res.get("stage_us", {})
         per_rows, dom_bytes, dom_time, launches = [], 0.0, 0.0, 0
+        dom_flops = 0.0
         for t, us in zip(tokens, res["per_t"]):
             ids = res["inputs"][t]["topk_ids"].numpy()
             b = traffic.layer_bytes(ids, *dims)
             f = traffic.layer_flops(ids, *dims)
-            plan = _lib.launch_plan(t, shape.top_k, res["n_local"], shape.hidden, shape.inter)
+            plan = _lib.launch_plan(t, shape.top_k, res["n_local"], shape.hidden, shape.inter, shape.n_experts)
             launches += plan["launches"] + (1 if world > 1 else 0)   # + the exchange kernel
             gbs = b / (us * 1e-6) / 1e9
             row = {"T": t, "us": round(us, 3), "bytes": b, "flops": f, "GBps": round(gbs, 1),
@@ -633,6 +640,7 @@ class Bench:
                     row.update({"kernels_us": {"layer": round(k1, 3)},
                                 "layer_kernel_GBps": round(b / (k1 * 1e-6) / 1e9, 1)})
                     dom_bytes += b
+                    dom_flops += f
                     dom_time += k1
                 else:
                     b1 = traffic.gemm1_bytes(ids, *dims)
@@ -641,12 +649,15 @@ class Bench:
                                                "gemm2": round(k2, 3), "combine": round(comb, 3)},
                                 "gemm1_GBps": round(b1 / (k1 * 1e-6) / 1e9, 1),
                                 "gemm2_GBps": round(b2 / (k2 * 1e-6) / 1e9, 1)})
+                    f1 = traffic.gemm1_flops(ids, *dims)
+                    row["gemm1_TFLOPs"] = round(f1 / (k1 * 1e-6) / 1e12, 1)
                     dom_bytes += b1
+                    dom_flops += f1
                     dom_time += k1
             if "rank_split" in res:
                 row["ranks"] = res["rank_split"][str(t)]
             per_rows.append(row)
-        return per_rows, dom_bytes, dom_time, launches
+        return per_rows, dom_bytes, dom_time, launches, dom_flops
 
 
 def traffic_record(name):
@@ -658,17 +669,27 @@ def traffic_record(name):
 
 def run_muse(args, world, rank, local):
     b = Bench(args, world, rank, local)
-    shape, tokens = sweep(b.synth, args.workload, args.tokens)
+    shape, tokens = sweep(b.synth, args.workload, args.tokens, args.experts)
     res = b.measure(args.workload, tokens, full=True)
-    per_rows, dom_bytes, dom_time, launches = b.rows(res)
+    per_rows, dom_bytes, dom_time, launches, dom_flops = b.rows(res)
     per_t = res["per_t"]
     pk = peaks()
+    bound, unit = "hbm", "GB/s"
     if world == 1:
-        achieved = dom_bytes / (dom_time * 1e-6) / 1e9
         roof_kernel = ("expert_gemm_tc launch of each call's dominant kernel (the single fused "
-                       "layer kernel for decode batches, else GEMM1): algorithmic bytes per launch / "
+                       "layer kernel for decode batches, else GEMM1): algorithmic {} per launch / "
                        "mean CUDA-event duration, summed over the token sweep")
-        roof_peak = pk["hbm_gbs"]
+        # the bound whose roofline time is longer: weight bytes at HBM bandwidth, or the MMA
+        # FLOPs at the sustained bf16 peak (the dominant kernels of prefill run for milliseconds)
+        if dom_flops / (pk["bf16_tflops_sustained"] * 1e12) > dom_bytes / (pk["hbm_gbs"] * 1e9):
+            bound, unit = "tensor", "TFLOP/s"
+            achieved = dom_flops / (dom_time * 1e-6) / 1e12
+            roof_peak = pk["bf16_tflops_sustained"]
+            roof_kernel = roof_kernel.format("FLOPs") + ", against the sustained bf16 peak"
+        else:
+            achieved = dom_bytes / (dom_time * 1e-6) / 1e9
+            roof_peak = pk["hbm_gbs"]
+            roof_kernel = roof_kernel.format("bytes")
     else:
         # whole expert-parallel call: every rank's algorithmic bytes over the slowest rank's
         # time, against N GPUs' bandwidth
@@ -686,7 +707,7 @@ def run_muse(args, world, rank, local):
         "data": "synthetic (seeded; random-init NVFP4 weights)",
         "config": config_block(args.workload, shape, tokens, world),
         "per_T": per_rows,
-        "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": roof_peak, "unit": "GB/s",
+        "roofline": {"bound": bound, "achieved": round(achieved, 1), "peak": roof_peak, "unit": unit,
                      "frac": round(achieved / roof_peak, 4),
                      "traffic": tr["bytes_per_launch"] if tr else None,
                      "peak_source": pk["source"], "kernel": roof_kernel},
@@ -707,10 +728,11 @@ def run_muse(args, world, rank, local):
             "value_minus_floor": round(geomean([v - fl for v in rd]), 3)}
     if "cpu_baseline" in res and rank == 0:
         line["cpu_baseline"] = res["cpu_baseline"]
-    if world == 1 and not args.no_secondary and args.workload == DEFAULT_WORKLOAD and args.tokens is None:
+    if (world == 1 and not args.no_secondary and args.workload == DEFAULT_WORKLOAD and args.tokens is None
+            and args.experts is None):
         s_shape, s_tokens = sweep(b.synth, SECONDARY_WORKLOAD, None)
         sres = b.measure(SECONDARY_WORKLOAD, s_tokens, full=False)
-        s_rows, s_bytes, s_time, _ = b.rows(sres)
+        s_rows, s_bytes, s_time, _, _ = b.rows(sres)
         line["secondary"] = {SECONDARY_WORKLOAD: {
             "config": config_block(SECONDARY_WORKLOAD, s_shape, s_tokens, world)["workload"],
             "value": round(geomean(sres["per_t"]), 3), "unit": "us/call", "per_T": s_rows,

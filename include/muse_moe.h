@@ -136,6 +136,28 @@ int muse_moe_forward(const void* x, const int32_t* topk_ids, const float* topk_w
                      void* workspace, size_t workspace_bytes, muse_stream_t stream);
 
 /*
+ * muse_moe_forward with every option in one call:
+ *   n_experts     experts in the whole model (the reference's Config n_experts, baseline.py:
+ *                 37-44); local_count of them are computed here. The batch's pairs spread over
+ *                 all n_experts, so a local expert expects T*K / n_experts of them: the token
+ *                 tile, and with it the kernels' pipeline layout, is chosen from that (on an
+ *                 expert-parallel slice T*K / local_count would overstate it R-fold). 0 means
+ *                 local_count (what muse_moe_forward assumes). Results do not depend on it.
+ *   out_f32       0: out is bf16 [T, H] (muse_moe_forward); 1: out is the fp32 sum before the
+ *                 cast (muse_moe_forward_partial).
+ *   stage_events  NULL, or five CUDA events recorded as in muse_moe_forward_profiled.
+ * Replaces kernel_fn (baseline.py:106-151), like muse_moe_forward.
+ */
+int muse_moe_forward_ex(const void* x, const int32_t* topk_ids, const float* topk_weights,
+                        int tokens, int top_k, int local_start, int local_count, int n_experts,
+                        int hidden, int inter,
+                        const uint8_t* w13p, const uint8_t* w13_sfp, const float* w13_gs,
+                        const uint8_t* w2p, const uint8_t* w2_sfp, const float* w2_gs,
+                        const void* post_norm_w, void* out, int out_f32,
+                        void* workspace, size_t workspace_bytes, muse_stream_t stream,
+                        void* const* stage_events);
+
+/*
  * One expert-parallel rank's share of the layer: muse_moe_forward for the local experts
  * [local_start, local_start + local_count), but `out_f32` (fp32 [T, H]) receives the fp32 sum
  * over this rank's local slots of topk_weight * norm(y), before any bf16 rounding (zeros for
@@ -248,6 +270,10 @@ int muse_moe_forward_profiled(const void* x, const int32_t* topk_ids, const floa
  */
 int muse_moe_launch_plan(int tokens, int top_k, int local_count, int hidden, int inter,
                          int* plan);
+
+/* muse_moe_launch_plan for a call of muse_moe_forward_ex with n_experts (0 = local_count). */
+int muse_moe_launch_plan_ex(int tokens, int top_k, int local_count, int n_experts, int hidden,
+                            int inter, int* plan);
 
 /*
  * muse_moe_forward without a workspace argument: it allocates nothing and takes its scratch

@@ -31,6 +31,10 @@ SIGNATURES: dict[str, tuple] = {
                                        _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P,
                                        ctypes.POINTER(_P)]),
     "muse_moe_launch_plan": (_I, [_I, _I, _I, _I, _I, ctypes.POINTER(_I)]),
+    "muse_moe_launch_plan_ex": (_I, [_I, _I, _I, _I, _I, _I, ctypes.POINTER(_I)]),
+    "muse_moe_forward_ex": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I,
+                                 _P, _P, _P, _P, _P, _P, _P, _P, _I, _P, ctypes.c_size_t, _P,
+                                 ctypes.POINTER(_P)]),
     "muse_moe_forward_partial": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I,
                                       _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P]),
     "muse_moe_cast_bf16": (_I, [_P, _P, ctypes.c_size_t, _P]),
@@ -125,9 +129,11 @@ def workspace_size(tokens: int, top_k: int, local_count: int, hidden: int, inter
     return int(n.value)
 
 
-def launch_plan(tokens: int, top_k: int, local_count: int, hidden: int, inter: int) -> dict:
-    """Kernels, token tile, stages and routing mode of one forward call (include/muse_moe.h)."""
+def launch_plan(tokens: int, top_k: int, local_count: int, hidden: int, inter: int,
+                n_experts: int = 0) -> dict:
+    """Kernels, token tile, stages and routing mode of one forward call (include/muse_moe.h);
+    n_experts: experts in the whole model (0: local_count)."""
     arr = (ctypes.c_int * 5)()
-    call("muse_moe_launch_plan", tokens, top_k, local_count, hidden, inter, arr)
+    call("muse_moe_launch_plan_ex", tokens, top_k, local_count, n_experts, hidden, inter, arr)
     return {"launches": arr[0], "n_box": arr[1], "stages": arr[2], "path": int(arr[3]),
             "fused": arr[3] == 2, "route_inline": arr[3] >= 1, "pair_tiles": bool(arr[4])}

@@ -60,9 +60,13 @@ int check_dims(int tokens, int top_k, int local_start, int local_count, int hidd
   return MUSE_OK;
 }
 
-// Token tile (the MMA's N) from the expected pairs per local expert; shapes only.
-int pick_n_box(int tokens, int top_k, int local_count) {
-  const long long per_expert = 2LL * tokens * top_k / local_count;
+// Token tile (the MMA's N) from the expected pairs per local expert (twice the mean, so that
+// most experts fit one tile); shapes only. The batch's T*K pairs spread over the model's
+// n_experts experts, of which this call computes local_count, so a local expert expects
+// T*K / n_experts of them -- on an expert-parallel slice (n_experts = R * local_count) R times
+// fewer than T*K / local_count.
+int pick_n_box(int tokens, int top_k, int n_experts) {
+  const long long per_expert = 2LL * tokens * top_k / n_experts;
   int n = 16;
   while (n < 128 && n < per_expert) n <<= 1;
   return n;
@@ -71,9 +75,8 @@ int pick_n_box(int tokens, int top_k, int local_count) {
 // Pair-tile items (one dequantised weight chunk feeds two 128-token tiles): when the batch
 // averages at least 128 pairs per local expert, i.e. most of its pairs sit in experts with two
 // or more full tiles (prefill); shapes only.
-bool use_pair_tiles(int tokens, int top_k, int local_count) {
-  return pick_n_box(tokens, top_k, local_count) == 128 &&
-         (long long)tokens * top_k >= 128LL * local_count;
+bool use_pair_tiles(int tokens, int top_k, int n_experts) {
+  return pick_n_box(tokens, top_k, n_experts) == 128 && (long long)tokens * top_k >= 128LL * n_experts;
 }
 
 // The single-launch (fused) path: decode batches of at most kMaxFusedPairs pairs with a small
@@ -84,9 +87,9 @@ constexpr int kMaxFusedPairs = 128;
 // Launch plan of a call: 2 = the whole layer in one cooperative launch, 1 = GEMM1 routes in
 // its prologue and gathers x itself (then GEMM2, combine), 0 = route, gather, GEMM1, GEMM2,
 // combine.
-int path_of(int tokens, int top_k, int local_count) {
+int path_of(int tokens, int top_k, int n_experts) {
   const long long pairs = (long long)tokens * top_k;
-  if (pick_n_box(tokens, top_k, local_count) > kMaxInlineBox || pairs > kMaxInlinePairs) return 0;
+  if (pick_n_box(tokens, top_k, n_experts) > kMaxInlineBox || pairs > kMaxInlinePairs) return 0;
   return pairs <= kMaxFusedPairs ? 2 : 1;
 }
 
@@ -190,15 +193,18 @@ extern "C" int muse_moe_prepare_weights(const uint8_t* w13, const uint8_t* w13_s
 namespace {
 
 // The launch sequence of one layer call. `ev` (optional) receives five event records on the
-// stream: start, before GEMM1, after GEMM1, after GEMM2, after the combine.
+// stream: start, before GEMM1, after GEMM1, after GEMM2, after the combine. n_experts: the
+// model's expert count (for the tile choice; local_count when unknown).
 int forward_impl(const void* x, const int32_t* topk_ids, const float* topk_weights, int tokens,
                  int top_k, int local_start, int local_count, int hidden, int inter,
                  const uint8_t* w13p, const uint8_t* w13_sfp, const float* w13_gs,
                  const uint8_t* w2p, const uint8_t* w2_sfp, const float* w2_gs,
                  const void* post_norm_w, void* out, void* workspace, size_t workspace_bytes,
-                 cudaStream_t st, cudaEvent_t* ev, bool f32_out = false) {
+                 cudaStream_t st, cudaEvent_t* ev, bool f32_out = false, int n_experts = 0) {
   int rc = check_dims(tokens, top_k, local_start, local_count, hidden, inter);
   if (rc) return rc;
+  if (n_experts == 0) n_experts = local_count;
+  if (n_experts < local_count) return MUSE_ERR_INVALID_ARGUMENT;
   if (tokens == 0) return MUSE_OK;
   if (!x || !topk_ids || !topk_weights || !w13p || !w13_sfp || !w13_gs || !w2p || !w2_sfp ||
       !w2_gs || !post_norm_w || !out || !workspace)
@@ -224,9 +230,9 @@ int forward_impl(const void* x, const int32_t* topk_ids, const float* topk_weigh
   const LayerDims d{tokens, top_k, local_start, local_count, hidden, inter};
   const int P = d.n_pairs();
   const int rows = (int)pair_rows(tokens, top_k);
-  const int n_box = pick_n_box(tokens, top_k, local_count);
-  const int path = path_of(tokens, top_k, local_count);
-  const bool pair = path == 0 && use_pair_tiles(tokens, top_k, local_count);
+  const int n_box = pick_n_box(tokens, top_k, n_experts);
+  const int path = path_of(tokens, top_k, n_experts);
+  const bool pair = path == 0 && use_pair_tiles(tokens, top_k, n_experts);
   int b_stages = 0;
   const int stages = pick_stages(n_box, pair, &b_stages);
   auto mark = [&](int i) -> int { return ev ? (int)cudaEventRecord(ev[i], st) : 0; };
@@ -314,8 +320,10 @@ int forward_impl(const void* x, const int32_t* topk_ids, const float* topk_weigh
     g.route_inline = 1;
     gemm1.b_source = 1;  // four-row gathers of x
   } else {
-    if ((rc = launch_route(topk_ids, tokens, top_k, local_start, local_count, s.offsets,
-                           s.pair_order, s.pair_row, st)))
+    // large batches: the multi-CTA routing, its per-CTA counts in the head of ypart (written only
+    // later, by GEMM2)
+    if ((rc = launch_route_multi(topk_ids, tokens, top_k, local_start, local_count, s.offsets,
+                                 s.pair_order, s.pair_row, reinterpret_cast<int32_t*>(s.ypart), st)))
       return rc;
     if ((rc = launch_gather(static_cast<const uint16_t*>(x), s.offsets, s.pair_order, local_count,
                             top_k, P, hidden, s.xs, st)))
@@ -388,14 +396,16 @@ extern "C" int muse_moe_cast_bf16(const float* in, void* out, size_t n, muse_str
   return launch_cast_bf16(in, static_cast<uint16_t*>(out), n, (cudaStream_t)stream);
 }
 
-extern "C" int muse_moe_launch_plan(int tokens, int top_k, int local_count, int hidden, int inter,
-                                    int* plan) {
+extern "C" int muse_moe_launch_plan_ex(int tokens, int top_k, int local_count, int n_experts, int hidden,
+                                       int inter, int* plan) {
   if (!plan) return MUSE_ERR_INVALID_ARGUMENT;
   const int rc = check_dims(tokens, top_k, 0, local_count, hidden, inter);
   if (rc) return rc;
-  const int n_box = pick_n_box(tokens, top_k, local_count);
-  const int path = path_of(tokens, top_k, local_count);
-  const bool pair = path == 0 && use_pair_tiles(tokens, top_k, local_count);
+  if (n_experts == 0) n_experts = local_count;
+  if (n_experts < local_count) return MUSE_ERR_INVALID_ARGUMENT;
+  const int n_box = pick_n_box(tokens, top_k, n_experts);
+  const int path = path_of(tokens, top_k, n_experts);
+  const bool pair = path == 0 && use_pair_tiles(tokens, top_k, n_experts);
   plan[0] = tokens == 0 ? 0 : (path == 2 ? 1 : path == 1 ? 3 : 5);
   plan[1] = n_box;
   int b_stages = 0;
@@ -403,4 +413,30 @@ extern "C" int muse_moe_launch_plan(int tokens, int top_k, int local_count, int 
   plan[3] = path;
   plan[4] = pair;
   return MUSE_OK;
+}
+
+extern "C" int muse_moe_launch_plan(int tokens, int top_k, int local_count, int hidden, int inter,
+                                    int* plan) {
+  return muse_moe_launch_plan_ex(tokens, top_k, local_count, local_count, hidden, inter, plan);
+}
+
+extern "C" int muse_moe_forward_ex(const void* x, const int32_t* topk_ids, const float* topk_weights,
+                                   int tokens, int top_k, int local_start, int local_count,
+                                   int n_experts, int hidden, int inter, const uint8_t* w13p,
+                                   const uint8_t* w13_sfp, const float* w13_gs, const uint8_t* w2p,
+                                   const uint8_t* w2_sfp, const float* w2_gs,
+                                   const void* post_norm_w, void* out, int out_f32, void* workspace,
+                                   size_t workspace_bytes, muse_stream_t stream,
+                                   void* const* stage_events) {
+  cudaEvent_t ev[5];
+  if (stage_events) {
+    for (int i = 0; i < 5; ++i) {
+      if (!stage_events[i]) return MUSE_ERR_INVALID_ARGUMENT;
+      ev[i] = static_cast<cudaEvent_t>(stage_events[i]);
+    }
+  }
+  return forward_impl(x, topk_ids, topk_weights, tokens, top_k, local_start, local_count, hidden,
+                      inter, w13p, w13_sfp, w13_gs, w2p, w2_sfp, w2_gs, post_norm_w, out, workspace,
+                      workspace_bytes, (cudaStream_t)stream, stage_events ? ev : nullptr, out_f32 != 0,
+                      n_experts);
 }

@@ -16,7 +16,10 @@ namespace {
 constexpr int kThreads = 256;
 constexpr int kColsPerCta = kThreads * 4;
 
-// grid (tokens, ceil(H / 1024)). Warp w computes the coefficients of slots w, w + 8, ...
+// grid (tokens, column blocks): a CTA covers columns [blockIdx.y * 1024, ...) in steps of
+// gridDim.y * 1024, so with one column block it computes its token's coefficients once for the
+// whole row (large batches), with several the row's columns spread over CTAs (small batches).
+// Warp w computes the coefficients of slots w, w + 8, ...
 // kF32Out: write the fp32 sum (an expert-parallel rank's partial) instead of bf16.
 template <bool kF32Out>
 __global__ void __launch_bounds__(kThreads)
@@ -41,13 +44,13 @@ combine_kernel(const int32_t* __restrict__ ids, const float* __restrict__ topk_w
   __syncthreads();
   if (tid == 0) s_n = sort_local_slots(s_row, s_key, s_coef, top_k, s_order, s_srow, s_scoef);
   __syncthreads();
-  const int h4 = blockIdx.y * kThreads + tid;  // float4 column group
-  if (h4 * 4 >= H) return;
-  const float4 acc = weighted_rows(ypart, H, s_srow, s_scoef, s_n, h4);
-  if (kF32Out)
-    reinterpret_cast<float4*>(static_cast<float*>(out) + (size_t)t * H)[h4] = acc;
-  else
-    reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + (size_t)t * H)[h4] = pack_bf16x4(acc);
+  for (int h4 = blockIdx.y * kThreads + tid; h4 * 4 < H; h4 += gridDim.y * kThreads) {  // float4 groups
+    const float4 acc = weighted_rows(ypart, H, s_srow, s_scoef, s_n, h4);
+    if (kF32Out)
+      reinterpret_cast<float4*>(static_cast<float*>(out) + (size_t)t * H)[h4] = acc;
+    else
+      reinterpret_cast<uint2*>(static_cast<uint16_t*>(out) + (size_t)t * H)[h4] = pack_bf16x4(acc);
+  }
 }
 
 // out[i] = bf16(in[i]), 8 elements per thread (n a multiple of 8).
@@ -65,7 +68,9 @@ cast_bf16_kernel(const float4* __restrict__ in, uint4* __restrict__ out, size_t 
 
 int launch_combine(const LayerDims& d, const int32_t* ids, const float* topk_weights,
                    const Scratch& s, void* out, bool f32_out, cudaStream_t stream) {
-  dim3 grid(d.tokens, (d.hidden + kColsPerCta - 1) / kColsPerCta);
+  // small batches spread a row over CTAs (latency); from 1024 tokens on, one CTA per token
+  // (its coefficients -- K rows of H/32 slice sums -- are read once, not once per column block)
+  dim3 grid(d.tokens, d.tokens >= 1024 ? 1 : (d.hidden + kColsPerCta - 1) / kColsPerCta);
   if (f32_out)
     combine_kernel<true><<<grid, kThreads, 0, stream>>>(ids, topk_weights, s.pair_row, s.ypart,
                                                          s.ssq, d.top_k, d.hidden, out);

@@ -98,6 +98,12 @@ constexpr int kMaxInlineBox = 32;
 int launch_route(const int32_t* ids, int tokens, int top_k, int local_start, int local_count,
                  int32_t* offsets, int32_t* pair_order, int32_t* pair_row, cudaStream_t stream);
 
+// The same routing by several CTAs for large batches; `scratch` holds route_scratch_bytes().
+size_t route_scratch_bytes(int n_pairs, int local_count);
+int launch_route_multi(const int32_t* ids, int tokens, int top_k, int local_start, int local_count,
+                       int32_t* offsets, int32_t* pair_order, int32_t* pair_row, int32_t* scratch,
+                       cudaStream_t stream);
+
 int launch_gather(const uint16_t* x, const int32_t* offsets, const int32_t* pair_order, int n_local,
                   int top_k, int max_rows, int hidden, uint16_t* xs, cudaStream_t stream);
 

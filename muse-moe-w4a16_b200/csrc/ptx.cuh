@@ -6,6 +6,8 @@
 #include <cuda.h>
 #include <stdint.h>
 
+#include "trace.cuh"
+
 namespace muse {
 namespace ptx {
 
@@ -79,9 +81,11 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
 // sleeps in the barrier instead of polling, leaving the issue slots to the other warps.
 __device__ __forceinline__ bool mbar_wait_sleep(uint64_t* bar, uint32_t parity) {
   if (mbar_try_wait(bar, parity)) return true;
+  MUSE_TRACE_WAIT_ENTER();
   const long long t0 = clock64();
   for (;;) {
     if (mbar_try_wait_sleep(bar, parity, 20000)) return true;
+    MUSE_TRACE_WAIT_ITER();
     if (clock64() - t0 > kWaitCycles) return false;
   }
 }

@@ -26,7 +26,8 @@ constexpr int kTrA = kTrF + 3 * kTrC;
 constexpr int kTrM = kTrA + 3 * kTrC;
 constexpr int kTrB = kTrM + 3 * kTrC;
 constexpr int kTrE = kTrB + 3 * kTrC;
-constexpr int kTraceStride = kTrE + 2 * kTrJ;
+constexpr int kTrWait = kTrE + 2 * kTrJ;   // per warp: wait-loop iterations (32), waits entered (32)
+constexpr int kTraceStride = kTrWait + 64;
 
 }  // namespace trace
 }  // namespace muse
@@ -50,8 +51,14 @@ __device__ __forceinline__ void stamp_global_entry() {
     g_trace_buf[(size_t)blockIdx.x * kTraceStride + 1] = clock64();
   }
 }
+__device__ __forceinline__ void count_wait(int which) {
+  if (g_trace_buf && (threadIdx.x & 31) == 0)
+    atomicAdd(&g_trace_buf[(size_t)blockIdx.x * kTraceStride + kTrWait + 32 * which + (threadIdx.x >> 5)], 1ull);
+}
 }  // namespace trace
 }  // namespace muse
+#define MUSE_TRACE_WAIT_ITER() ::muse::trace::count_wait(0)
+#define MUSE_TRACE_WAIT_ENTER() ::muse::trace::count_wait(1)
 #define MUSE_TRACE_ENTRY() ::muse::trace::stamp_global_entry()
 #define MUSE_TRACE_AT(slot) ::muse::trace::stamp(slot)
 #define MUSE_TRACE_SEQ(base, p, c)                                              \
@@ -63,6 +70,8 @@ __device__ __forceinline__ void stamp_global_entry() {
     if ((j) < ::muse::trace::kTrJ) ::muse::trace::stamp((base) + (j));          \
   } while (0)
 #else
+#define MUSE_TRACE_WAIT_ITER() ((void)0)
+#define MUSE_TRACE_WAIT_ENTER() ((void)0)
 #define MUSE_TRACE_ENTRY() ((void)0)
 #define MUSE_TRACE_AT(slot) ((void)0)
 #define MUSE_TRACE_SEQ(base, p, c) ((void)0)

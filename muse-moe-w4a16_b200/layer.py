@@ -93,9 +93,10 @@ def prepare(weights: Weights, experts: range | None = None) -> dict:
 
 
 def _call_args(data: Inputs, state: dict, out: torch.Tensor | None, workspace: torch.Tensor | None,
-               out_dtype: torch.dtype):
-    """Validated pointers and sizes of one layer call (the argument list shared by
-    muse_moe_forward, _profiled and _partial), plus the output tensor."""
+               out_dtype: torch.dtype, stage_events: list | None = None):
+    """Validated argument list of muse_moe_forward_ex for one layer call, plus the output tensor.
+    config["n_experts"] (the model's expert count, baseline.py:37-44) sizes the token tile; a
+    missing or inconsistent value falls back to the local count."""
     cfg = data["config"]
     x = data["hidden_states"]
     _require_cuda(x, "hidden_states")
@@ -128,12 +129,24 @@ def _call_args(data: Inputs, state: dict, out: torch.Tensor | None, workspace: t
     e0 = lo - base
     w13_e, w13sf_e = 2 * I * H // 2, 2 * I * H // 16     # bytes per expert
     w2_e, w2sf_e = H * I // 2, H * I // 16
-    args = (_ptr(x), _ptr(ids), _ptr(wts), T, K, lo, cnt, H, I,
+    n_experts = int(cfg.get("n_experts", 0) or 0)
+    if n_experts < lo + cnt:
+        n_experts = 0
+    ev = None
+    if stage_events is not None:
+        if len(stage_events) != 5:
+            raise _lib.MuseError(_lib.MUSE_ERR_INVALID_ARGUMENT, "stage_events needs five CUDA events")
+        for e in stage_events:   # torch creates the CUDA event on its first record
+            if not e.cuda_event:
+                e.record()
+        ev = (ctypes.c_void_p * 5)(*(e.cuda_event for e in stage_events))
+    args = (_ptr(x), _ptr(ids), _ptr(wts), T, K, lo, cnt, n_experts, H, I,
             _ptr(state["w13"], e0 * w13_e), _ptr(state["w13_sf"], e0 * w13sf_e),
             _ptr(state["w13_gs"], e0 * 4),
             _ptr(state["w2"], e0 * w2_e), _ptr(state["w2_sf"], e0 * w2sf_e),
             _ptr(state["w2_gs"], e0 * 4),
-            _ptr(state["post_norm_w"]), _ptr(out), _ptr(ws), ws_bytes, _stream(dev))
+            _ptr(state["post_norm_w"]), _ptr(out), 1 if out_dtype == torch.float32 else 0,
+            _ptr(ws), ws_bytes, _stream(dev), ev)
     return args, out
 
 
@@ -144,17 +157,8 @@ def kernel_fn(data: Inputs, state: dict, out: torch.Tensor | None = None,
     `out` and `workspace` (uint8, >= workspace_size bytes) may be supplied by the caller.
     `stage_events` (five torch.cuda.Event(enable_timing=True)) are recorded around the kernels:
     start, before GEMM1, after GEMM1, after GEMM2, after the combine."""
-    args, out = _call_args(data, state, out, workspace, torch.bfloat16)
-    if stage_events is None:
-        _lib.call("muse_moe_forward", *args)
-    else:
-        if len(stage_events) != 5:
-            raise _lib.MuseError(_lib.MUSE_ERR_INVALID_ARGUMENT, "stage_events needs five CUDA events")
-        for e in stage_events:   # torch creates the CUDA event on its first record
-            if not e.cuda_event:
-                e.record()
-        ev = (ctypes.c_void_p * 5)(*(e.cuda_event for e in stage_events))
-        _lib.call("muse_moe_forward_profiled", *args, ev)
+    args, out = _call_args(data, state, out, workspace, torch.bfloat16, stage_events)
+    _lib.call("muse_moe_forward_ex", *args)
     return out
 
 
@@ -164,7 +168,7 @@ def kernel_fn_partial(data: Inputs, state: dict, out: torch.Tensor | None = None
     the sum over local slots before the bf16 cast; zeros for tokens with no local pair. The sum
     of every rank's share, cast to bf16, is kernel_fn's output over all experts."""
     args, out = _call_args(data, state, out, workspace, torch.float32)
-    _lib.call("muse_moe_forward_partial", *args)
+    _lib.call("muse_moe_forward_ex", *args)
     return out
 
 

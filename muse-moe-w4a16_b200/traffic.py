@@ -50,3 +50,9 @@ def gemm2_bytes(topk_ids, local_start: int, local_count: int, hidden: int, inter
     rows and sums of squares it writes."""
     pairs, used = _pairs_and_experts(topk_ids, local_start, local_count)
     return int(used * weight_bytes(hidden, inter) + 2 * pairs * inter + 4 * pairs * hidden + 4 * pairs)
+
+
+def gemm1_flops(topk_ids, local_start: int, local_count: int, hidden: int, inter: int) -> int:
+    """GEMM1 launch: 2 * pairs * 2I * H."""
+    pairs, _ = _pairs_and_experts(topk_ids, local_start, local_count)
+    return 2 * pairs * 2 * inter * hidden

@@ -146,3 +146,16 @@ def test_peer_allreduce_rejects_bad_arguments(lib):
     assert f(s0, s1, flags, 2, 0, 64, None, None) == bad                # no output
     assert f(u64(0x1000, 0), s1, flags, 2, 0, 64, out, None) == bad     # null peer share
     assert f(u64(0x1004, 0x2000), s1, flags, 2, 0, 64, out, None) == bad  # misaligned share
+
+
+def test_launch_plan_counts_only_local_pairs_per_expert(pkg):
+    """On an expert-parallel slice the token tile follows the pairs a local expert can expect
+    (T*K / model experts), not T*K / local experts: the reference problem's ep8 slice at bs 256
+    keeps the 16-token decode tile; an unsharded call of the same size per expert does not."""
+    from muse_moe_w4a16_b200 import _lib
+    ep = _lib.launch_plan(256, 8, 32, 4096, 4096, 256)
+    whole = _lib.launch_plan(256, 8, 32, 4096, 4096)
+    assert ep["n_box"] == 16 and whole["n_box"] == 128
+    assert _lib.launch_plan(256, 8, 32, 4096, 4096, 0) == whole
+    with pytest.raises(Exception):
+        _lib.launch_plan(256, 8, 32, 4096, 4096, 16)   # fewer model experts than local ones

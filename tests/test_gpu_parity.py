@@ -142,7 +142,7 @@ def test_layer_pair_tile_items(pkg, synth, T, K, E, lo, cnt):
     tiles end with a one-tile item. Every row against the oracle."""
     from muse_moe_w4a16_b200 import _lib
     H, I = 256, 384
-    assert _lib.launch_plan(T, K, cnt, H, I)["pair_tiles"]
+    assert _lib.launch_plan(T, K, cnt, H, I, E)["pair_tiles"]
     shape = synth.MoEShape(E, K, H, I, local_start=lo, local_count=cnt, router="zipf")
     w = synth.baseline_weights(shape, seed=T + E)
     err, _ = _check_layer(pkg, w, synth.baseline_input(shape, T, seed=T))
@@ -283,12 +283,14 @@ def test_stage_outputs_match_oracle(pkg, synth):
 
 
 @pytest.mark.parametrize("T,E,K,lo,cnt", [(16, 8, 2, 0, 8), (128, 256, 8, 0, 256), (33, 256, 8, 32, 32),
-                                          (300, 256, 8, 0, 256)])
+                                          (300, 256, 8, 0, 256), (1100, 256, 8, 0, 256),
+                                          (4000, 64, 4, 16, 32)])
 def test_published_routing_and_dirty_workspace(pkg, synth, T, E, K, lo, cnt):
     """Batches of <= 1024 pairs with small token tiles are routed inside the first GEMM, larger
-    ones by the route kernel; either way the workspace ends up holding the oracle's routing,
-    bit-exact, and the output is right even when the workspace starts full of garbage (nothing
-    in it is read before the same call has written it)."""
+    ones by the route kernels (one CTA, or several CTAs of 4096 pairs each from 4097 pairs on);
+    either way the workspace ends up holding the oracle's routing, bit-exact, and the output is
+    right even when the workspace starts full of garbage (nothing in it is read before the same
+    call has written it)."""
     from muse_moe_w4a16_b200 import _lib
     H, I = 256, 256
     shape = synth.MoEShape(E, K, H, I, local_start=lo, local_count=cnt, router="uniform")
