@@ -633,27 +633,8 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     Item t_next;
     float gs_next = 0.f, pnw_next = 0.f;
     if (blockIdx.x < total) item_consts(blockIdx.x, t_next, gs_next, pnw_next);
-    // Single launch: this warp's GEMM1 rows are published once, after its last GEMM1 item (one
-    // GPU-scope fence, then a relaxed increment of each item's token-tile counter), and its
-    // GEMM2 rows once, after its last item (one increment of the completion counter). The warp
-    // barrier orders every lane's stores before lane 0's fence.
-    bool gemm1_published = !kFused || a.ph[0].signal == nullptr;
-    auto publish_gemm1 = [&](int j_end) {
-      __syncwarp();
-      if (lane == 0) {
-        __threadfence();
-        for (int jj = 0; jj < j_end; ++jj) {
-          const Item ti = decode_item<kPair>(ctl, offs, blockIdx.x + jj * G, n0, n_local, n_box, mt0, mt1);
-          ptx::red_relaxed_gpu_add(a.ph[0].signal + ti.tile, 1);
-        }
-      }
-      __syncwarp();
-      gemm1_published = true;
-    };
     int jm = 0;
-    int j = 0;
-    for (; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
-      if (!gemm1_published && blockIdx.x + j * G >= n0) publish_gemm1(j);
+    for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
       const Item t = t_next;
       const float gs_item = gs_next, pnw_item = pnw_next;
       if (blockIdx.x + (j + 1) * G < total) item_consts(blockIdx.x + (j + 1) * G, t_next, gs_next, pnw_next);
@@ -763,6 +744,14 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
         ptx::tc_fence_before();
         if (q == 0 && lane == 0) MUSE_TRACE_ITEM(trace::kTrE + trace::kTrJ, j);
         __syncwarp();
+        // Single launch: this warp's rows of a GEMM1 item are published as soon as they are
+        // stored (a CTA's items belong to different experts, so waiting for its last GEMM1 item
+        // would hold back GEMM2 items that depend only on the first). The warp barrier orders
+        // every lane's stores before lane 0's release.
+        if (kFused && t.ph == 0 && a.ph[0].signal) {
+          if (lane == 0) ptx::red_release_gpu_add(a.ph[0].signal + t.tile, 1);
+          __syncwarp();
+        }
 #pragma unroll
         for (int p = 0; p < kPipes; ++p) {
           if (chunk_begin(p, jm, f, split) >= kcn) continue;
@@ -771,14 +760,12 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
         }
       }
     }
-    if (kFused && ok) {
-      if (!gemm1_published) publish_gemm1(j);
-      if (a.ph[1].signal) {
-        __syncwarp();
-        if (lane == 0) {
-          __threadfence();
-          ptx::red_relaxed_gpu_add(a.ph[1].signal, 1);
-        }
+    // Single launch: one increment of the GEMM2 completion counter per warp, after its last item.
+    if (kFused && ok && a.ph[1].signal) {
+      __syncwarp();
+      if (lane == 0) {
+        __threadfence();
+        ptx::red_relaxed_gpu_add(a.ph[1].signal, 1);
       }
     }
     if (!ok && lane == 0) record_error(a.error_flag, 3);
