@@ -193,18 +193,27 @@ __device__ __forceinline__ void record_error(int* flag, int code) {
   if (flag) atomicExch(flag, code);
 }
 
-// The layer's combine for the tokens of this CTA (fused launches): out[t] = sum over t's local
-// slots, in ascending expert order, of topk_weight * rsqrt(mean(ypart^2) + eps) * ypart, fp32,
-// then bf16 (or fp32 for an expert-parallel share). Restates reference.py:88-90,106-107 with
-// combine.cu's arithmetic. A token's slots are found and ordered from the routing tables before
-// the rows exist; then one wait on the GEMM2 completion counter (every epilogue warp of every
-// CTA adds 1 after its last item), and the rows' sums of squares and values are read together.
+// The layer's combine (fused launches): out[t] = sum over t's local slots, in ascending expert
+// order, of topk_weight * rsqrt(mean(ypart^2) + eps) * ypart, fp32, then bf16 (or fp32 for an
+// expert-parallel share). Restates reference.py:88-90,106-107 with combine.cu's arithmetic.
+// The work is (token, column range) pieces, piece i to CTA i % G: with fewer tokens than CTAs a
+// token's columns are cut into ranges so that the whole grid combines it (each piece recomputes
+// the token's coefficients, which are read from the rows' slice sums of squares). A token's
+// slots are found and ordered from the routing tables before the rows exist; then one wait on
+// the GEMM2 completion counter (every epilogue warp of every CTA adds 1 after its last item),
+// and the rows' sums of squares and values are read together.
 __device__ __forceinline__ void combine_tokens(SharedCtl& ctl, const GemmArgs& a, int n_local) {
-  const int K = a.top_k, H = a.hidden;
+  const int K = a.top_k, H = a.hidden, H4 = H >> 2;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int total_rows = ctl.offs[n_local];
+  const int G = gridDim.x;
+  // column ranges per token (at least 8 float4 columns each) and their width in float4 columns
+  const int ranges = a.tokens >= G ? 1 : max(1, min(G / a.tokens, H4 / 8));
+  const int width = (H4 + ranges - 1) / ranges;
   bool waited = false;
-  for (int t = blockIdx.x; t < a.tokens; t += gridDim.x) {
+  for (int piece = blockIdx.x; piece < a.tokens * ranges; piece += G) {
+    const int t = piece / ranges;
+    const int h4_begin = (piece - t * ranges) * width, h4_end = min(H4, h4_begin + width);
     if (threadIdx.x < K) {
       ctl.c_row[threadIdx.x] = -1;
       ctl.c_key[threadIdx.x] = a.ids[t * K + threadIdx.x];
@@ -227,9 +236,9 @@ __device__ __forceinline__ void combine_tokens(SharedCtl& ctl, const GemmArgs& a
     }
     // The rows' values are loaded while the coefficients are being computed. Every thread makes
     // the same number of passes (the barrier inside), and only those with a column group work.
-    for (int base4 = 0; base4 * 4 < H; base4 += blockDim.x) {
+    for (int base4 = h4_begin; base4 < h4_end; base4 += blockDim.x) {
       const int h4 = base4 + threadIdx.x;
-      const bool mine = h4 * 4 < H;
+      const bool mine = h4 < h4_end;
       // the first eight rows are in flight across the barrier; more slots (top_k > 8) follow
       float4 v[8];
 #pragma unroll
@@ -314,6 +323,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
       ptx::mbar_init(&pc.drain, 1);
     }
     ptx::fence_barrier_init();
+    MUSE_TRACE_AT(5);
   }
   if (warp < kPipes && lane == 0) {
     ptx::prefetch_tensormap(a.route_inline ? &tmap_x : &tmap_b);
@@ -331,6 +341,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     }
     offs = ctl.offs;
   }
+  if (threadIdx.x == 0) MUSE_TRACE_AT(6);
   int incl = 0;  // item columns of experts [32 * warp, threadIdx.x], threads < 256
   if (threadIdx.x < 256) {
     const float f = e4m3_to_float(threadIdx.x) * 1152921504606846976.0f;  // * 2^60
@@ -355,9 +366,11 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
     ptx::tmem_alloc(&ctl.tmem_base, kTmemCols);
     ptx::tmem_relinquish();
   }
+  if (threadIdx.x == 0) MUSE_TRACE_AT(7);
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
+  if (threadIdx.x == 0) MUSE_TRACE_AT(8);
   if (a.route_inline) {  // pair index -> token and slot (CTA 0 has published the pair indices)
     for (int i = threadIdx.x; i < a.n_pairs; i += R::kThreads) {
       const int pr = ctl.order[i];
