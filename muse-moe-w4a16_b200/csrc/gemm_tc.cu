@@ -301,7 +301,28 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
   if (threadIdx.x == 0) MUSE_TRACE_ENTRY();
 
   // ---- set-up: barriers, scale table, work list, tensor memory
-  if (threadIdx.x == 0) {
+  auto init_barrier = [&](int p, int r) {  // barrier r of pipeline p's control block (single launch)
+    PipeCtl& pc = ctl.pipe[p];
+    if (r < Sw) return ptx::mbar_init(&pc.w_full[r], 1);
+    if ((r -= Sw) < Sw) return ptx::mbar_init(&pc.w_empty[r], DW);  // the dequant warps
+    if ((r -= Sw) < Sb) return ptx::mbar_init(&pc.b_full[r], 1);
+    if ((r -= Sb) < Sb) return ptx::mbar_init(&pc.b_empty[r], 1);  // MMA commit
+    if ((r -= Sb) < geo.n_a) return ptx::mbar_init(&pc.a_full[r], DW);
+    if ((r -= geo.n_a) < geo.n_a) return ptx::mbar_init(&pc.a_empty[r], 1);
+    if ((r -= geo.n_a) < geo.n_acc) return ptx::mbar_init(&pc.acc_full[r], 1);
+    if ((r -= geo.n_acc) < geo.n_acc) return ptx::mbar_init(&pc.acc_empty[r], 4);
+    ptx::mbar_init(&pc.drain, 1);
+  };
+  const int per_pipe = 2 * Sw + 2 * Sb + 2 * geo.n_a + 2 * geo.n_acc + 1;
+  if (kFused) {
+    // Single launch (latency-bound): the last warp initialises the barriers, one lane per
+    // barrier, while the first warps already load the routing ids.
+    if (warp == R::kWarps - 1) {
+      for (int i = lane; i < kPipes * per_pipe; i += 32) init_barrier(i / per_pipe, i % per_pipe);
+      ptx::fence_barrier_init();
+      if (lane == 0) MUSE_TRACE_AT(5);
+    }
+  } else if (threadIdx.x == 0) {
     for (int p = 0; p < kPipes; ++p) {
       PipeCtl& pc = ctl.pipe[p];
       for (int s = 0; s < Sw; ++s) {
@@ -428,6 +449,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
       // a time so that a satisfied dependency costs no round trip to L2.
       uint32_t dep_ready = 0;
       int dep_j0 = -64;
+      if (p == 0 && lane == 0) MUSE_TRACE_AT(9);
       int jm = 0;
       for (int j = 0; ok && blockIdx.x + j * G < total; ++j, jm = (jm + 1 == kPipes ? 0 : jm + 1)) {
         const int it = blockIdx.x + j * G;

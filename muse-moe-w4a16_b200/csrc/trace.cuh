@@ -6,8 +6,8 @@
 //
 //   [0] globaltimer at kernel entry (thread 0), [1] clock64 at entry, [2] set-up done,
 //   [3] every role done (before the tensor-memory release), [4] combine done,
-//   set-up steps (thread 0): [5] barriers initialised, [6] routing done, [7] scale table and
-//   tile scan issued, [8] first set-up barrier passed
+//   set-up steps: [5] barriers initialised (last warp), [6] routing done, [7] scale table and
+//   tile scan issued, [8] first set-up barrier passed (thread 0), [9] producer 0 starts
 //   producer p, chunk c: [kTrW + p*kTrC + c] weight tile issued, [kTrB + ...] activation issued
 //   dequant warp (lane quarter 0) of pipeline p: [kTrF + ...] weight tile landed,
 //                                                [kTrA + ...] A buffer handed to the MMA
