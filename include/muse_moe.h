@@ -240,6 +240,42 @@ int muse_moe_peer_reduce_scatter_bf16(const uint64_t* shares0, const uint64_t* s
                                       void* out, muse_stream_t stream);
 
 /*
+ * Prefill dispatch (tokens split over the ranks, tokens_per_rank = T_r on every rank): sends row
+ * t of this rank's x (bf16 [T_r, hidden]) to slot rank * T_r + t of rank d's receive buffer
+ * recv_x[d] (bf16 [ranks * T_r, hidden]) only when d owns one of the token's experts (rank d owns
+ * global expert ids [expert_start[d], expert_start[d + 1])), and the token's ids and weights to
+ * the same slot of every rank's recv_ids[d] / recv_weights[d] ([ranks * T_r, top_k]; the other
+ * ranks route it nowhere). masks (this rank's memory, uint32 [T_r]) receives each token's
+ * destination ranks as a bit mask, for muse_moe_peer_routed_reduce_scatter_bf16. The kernel
+ * then signals every rank and waits, bounded by timeout_us (0 = 1 s; expiry: device status 6),
+ * for all ranks' dispatch of the same generation, so this rank's receive buffers are complete
+ * when it finishes; then run muse_moe_forward_partial on them (ranks * T_r rows) and the routed
+ * reduce-scatter. Receive buffers and flags are peer mappings as for the exchange (flags: the
+ * same 32-word arrays; the generation is the exchange's). Replaces the all-gather of every
+ * token to every rank before the ep ranks' partial layers (reference.py:18-22, TASK.md:29).
+ */
+int muse_moe_ep_dispatch(const void* x, const int32_t* topk_ids, const float* topk_weights,
+                         int tokens_per_rank, int top_k, int hidden, int ranks, int rank,
+                         const int* expert_start, const uint64_t* recv_x, const uint64_t* recv_ids,
+                         const uint64_t* recv_weights, const uint64_t* flags, uint32_t* masks,
+                         long long timeout_us, muse_stream_t stream);
+
+/*
+ * The prefill exchange after muse_moe_ep_dispatch: out (bf16 [T_r, hidden], this rank) = for each
+ * of this rank's tokens t, the sum over the ranks in masks[t], in rank order, of row
+ * rank * T_r + t of their shares (fp32 [ranks * T_r, hidden], parity g & 1 as for the exchange).
+ * A rank whose experts the token does not use holds zeros in that row, so the result equals the
+ * full sum, but only the rows of the token's destination ranks cross NVLink.
+ * muse_moe_peer_exchange_bf16's flags, generation, parity check and bounded waits. Replaces the
+ * reduce-scatter of the ep ranks' partial outputs (reference.py:18-22, TASK.md:29).
+ */
+int muse_moe_peer_routed_reduce_scatter_bf16(const uint64_t* shares0, const uint64_t* shares1,
+                                             const uint64_t* flags, int ranks, int rank,
+                                             int tokens_per_rank, int hidden, const uint32_t* masks,
+                                             int expect_parity, long long timeout_us, void* out,
+                                             muse_stream_t stream);
+
+/*
  * muse_moe_forward, with five caller-created CUDA events (cudaEvent_t, passed as void*)
  * recorded on `stream` around the kernels: [0] start, [1] before GEMM1, [2] after GEMM1,
  * [3] after GEMM2, [4] after the combine. For per-kernel timing; same results as

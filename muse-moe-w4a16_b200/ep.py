@@ -18,11 +18,14 @@ Two layouts of the tokens:
       buffers (two rounds), so a rank reads ~1.5 x T x H x 4 bytes over NVLink instead of
       R x T x H x 4. (With CPU tensors, as in the gloo tests of the exchange logic, the shares
       are summed by an all-reduce collective instead.)
-  sharded (prefill): rank r holds its own T_r tokens (T_r equal on every rank). Inputs are
-      all-gathered (x bf16, ids, weights; NCCL), every rank writes its experts' share of all
-      R * T_r tokens into its symmetric buffer, and this library's peer kernel (reduce-scatter
-      mode) returns each rank the rank-ordered sum for its own tokens over NVLink. (CPU tensors:
-      a reduce-scatter collective, as in the gloo tests.)
+  sharded (prefill): rank r holds its own T_r tokens (T_r equal on every rank). This library's
+      dispatch kernel sends each token's row over NVLink only to the ranks that own one of its
+      experts (and its ids and weights to every rank), into fixed-capacity receive buffers of
+      R * T_r rows; every rank writes its experts' share of those R * T_r rows into its
+      symmetric buffer, and the routed reduce-scatter returns each rank, for each of its own
+      tokens, the rank-ordered sum over the token's destination ranks only (the other ranks'
+      rows are zero and never cross NVLink). (CPU tensors: an all-gather and a reduce-scatter
+      collective, as in the gloo tests.)
 
 Every exchange tells the kernel which share buffer (generation parity) the host wrote into; a
 disagreement with the device's count, or a peer that never signals within `timeout_us`, sets
@@ -92,7 +95,8 @@ class ExpertParallelMoE:
             local_fn = lambda d: kernel_fn_partial(d, self.state)  # noqa: E731
         self._local = local_fn
         self._cast = cast_fn or cast_bf16
-        self._peer = None   # symmetric buffers of the decode exchange, set up on first use
+        self._peer = None   # symmetric buffers of the exchange, set up on first use
+        self._recv = None   # symmetric receive buffers of the prefill dispatch, set up on first use
         self._gen = 0       # exchanges completed (the device keeps its own count; they agree)
         self.timeout_us = 0  # bound of the exchange's waits for the peers (0: the library's 1 s)
         # shares of at most this many bytes are summed whole by every rank (one flag round);
@@ -217,30 +221,75 @@ class ExpertParallelMoE:
         R = self.world
         if t_r == 0:   # T_r is the same on every rank: no rank exchanges anything
             return torch.empty((0, x.shape[1]), dtype=torch.bfloat16, device=x.device)
-        full = {}
-        for name, t in (("hidden_states", x), ("topk_ids", ids.to(torch.int32)),
-                        ("topk_weights", wts.to(torch.float32))):
-            t = t.contiguous()
-            g = torch.empty((R * t_r,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
-            dist.all_gather_into_tensor(g, t, group=self.group)
-            full[name] = g
-        gathered = _with_local_range({**data, **full}, self.experts)
         if not x.is_cuda or self.state is None:
+            full = {}
+            for name, t in (("hidden_states", x), ("topk_ids", ids.to(torch.int32)),
+                            ("topk_weights", wts.to(torch.float32))):
+                t = t.contiguous()
+                g = torch.empty((R * t_r,) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+                dist.all_gather_into_tensor(g, t, group=self.group)
+                full[name] = g
+            gathered = _with_local_range({**data, **full}, self.experts)
             part = self._local(gathered)
             mine = torch.empty((t_r, part.shape[1]), dtype=part.dtype, device=part.device)
             dist.reduce_scatter_tensor(mine, part, op=dist.ReduceOp.SUM, group=self.group)
             return self._cast(mine)
-        H = x.shape[1]
+        H, K = x.shape[1], ids.shape[1]
         self._peer_buffers(R * t_r * H, x.device)
-        parity = (self._gen + 1) & 1
+        recv = self._recv_buffers(R * t_r, H, K, x.device)
         peer = self._peer
+        parity = (self._gen + 1) & 1
+        masks = torch.empty(t_r, dtype=torch.int32, device=x.device)
+        ids32, wts32 = ids.to(torch.int32).contiguous(), wts.to(torch.float32).contiguous()
+        starts = (ctypes.c_int * (R + 1))(*[expert_block(self.n_experts, r, R).start for r in range(R)],
+                                          self.n_experts)
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        _lib.call("muse_moe_ep_dispatch", x.contiguous().data_ptr(), ids32.data_ptr(), wts32.data_ptr(),
+                  t_r, K, H, R, self.rank, starts, recv["x"], recv["ids"], recv["wts"], peer["flags"],
+                  masks.data_ptr(), int(self.timeout_us), stream)
+        n = R * t_r
+        received = _with_local_range({**data, "hidden_states": recv["x_local"][:n * H].view(n, H),
+                                      "topk_ids": recv["ids_local"][:n * K].view(n, K),
+                                      "topk_weights": recv["wts_local"][:n * K].view(n, K)}, self.experts)
         base = parity * peer["cap"]
-        share = peer["buf"][base:base + R * t_r * H].view(R * t_r, H)
-        kernel_fn_partial(gathered, self.state, out=share)
+        share = peer["buf"][base:base + n * H].view(n, H)
+        kernel_fn_partial(received, self.state, out=share)
         out = torch.empty((t_r, H), dtype=torch.bfloat16, device=x.device)
-        self._exchange(R * t_r * H, 1, parity, out)
+        _lib.call("muse_moe_peer_routed_reduce_scatter_bf16", peer["shares"][0], peer["shares"][1],
+                  peer["flags"], R, self.rank, t_r, H, masks.data_ptr(), parity, int(self.timeout_us),
+                  out.data_ptr(), stream)
         self._gen += 1
         return out
+
+    def _recv_buffers(self, rows: int, hidden: int, top_k: int, device) -> dict:
+        """Symmetric receive buffers of the prefill dispatch -- x rows (bf16 [rows, hidden]), ids
+        and weights ([rows, top_k]) -- of every rank, mapped into this one (collective: every
+        rank calls it with the same sizes; grown when a call needs more room)."""
+        need_x, need_k = rows * hidden, rows * top_k
+        if self._recv is not None and need_x <= self._recv["cap_x"] and need_k <= self._recv["cap_k"]:
+            return self._recv
+        import torch.distributed._symmetric_memory as symm
+        if self._recv is not None:   # growing: no rank may still be writing into the old buffers
+            torch.cuda.synchronize(device)
+            dist.barrier(group=self.group)
+        cap_x = (max(need_x, 1 << 16) + 127) // 128 * 128          # bf16 elements
+        cap_k = (max(need_k, 1 << 10) + 63) // 64 * 64              # int32 / fp32 elements
+        # [x: cap_x bf16 | ids: cap_k int32 | weights: cap_k fp32], in 4-byte words
+        words = cap_x // 2 + 2 * cap_k
+        buf = symm.empty(words, dtype=torch.int32, device=device)
+        handle = symm.rendezvous(buf, self.group if self.group is not None else dist.group.WORLD)
+        bases = [int(p) for p in handle.buffer_ptrs]
+        u64 = ctypes.c_uint64 * self.world
+        ids_at, wts_at = cap_x * 2, cap_x * 2 + cap_k * 4          # byte offsets
+        self._recv = {
+            "buf": buf, "handle": handle, "cap_x": cap_x, "cap_k": cap_k,
+            "x": u64(*bases), "ids": u64(*[b + ids_at for b in bases]), "wts": u64(*[b + wts_at for b in bases]),
+            "x_local": buf[:cap_x // 2].view(torch.bfloat16),
+            "ids_local": buf[cap_x // 2:cap_x // 2 + cap_k],
+            "wts_local": buf[cap_x // 2 + cap_k:].view(torch.float32),
+        }
+        dist.barrier(group=self.group)
+        return self._recv
 
 
 class DecodeGraphs:
