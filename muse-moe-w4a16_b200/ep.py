@@ -1,5 +1,6 @@
 """Expert parallelism across the GPUs of one node: one process per GPU, experts split into
-contiguous blocks; the decode exchange runs over NVLink peer memory, the prefill one on NCCL.
+contiguous blocks; the decode and prefill exchanges run over NVLink peer memory in this
+library's kernels (collectives only for CPU tensors).
 
 The reference's problem is always expert-parallel: GPU r holds experts
 [32r, 32r + 32) and computes only their (token, slot) pairs (reference.py:18-22, TASK.md:29).
