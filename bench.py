@@ -52,6 +52,10 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
 DEFAULT_WORKLOAD = "cfg4"
 SECONDARY_WORKLOAD = "cfg2"
 PARITY_TOL = 1.5e-2          # checks.compare's tolerance (reference.py:25)
+# Prefill workloads: at N > 1 their tokens are split evenly over the ranks (BASELINE cfg5: "T
+# split evenly across ranks") and each rank's call is the routed dispatch + partial layer +
+# routed reduce-scatter; the other workloads replicate the tokens (decode layout).
+PREFILL_WORKLOADS = ("cfg5",)
 # ncu per-launch DRAM traffic of the dominant kernel, recorded from the capture summarised in
 # profiles/ (read here so the line can carry it next to the algorithmic bytes)
 TRAFFIC_FILE = REPO / "profiles" / "traffic.json"
@@ -233,6 +237,15 @@ def metric_name(name):
     return f"MoE layer us/call (geomean over the token sweep), {name}"
 
 
+def shard(inp: dict, rank: int, world: int) -> dict:
+    """This rank's contiguous slice of a batch (T divisible by the rank count)."""
+    t = inp["hidden_states"].shape[0]
+    if t % world:
+        raise SystemExit(f"T={t} is not divisible by {world} ranks")
+    lo, hi = rank * t // world, (rank + 1) * t // world
+    return {k: (v[lo:hi] if isinstance(v, torch.Tensor) else v) for k, v in inp.items()}
+
+
 def config_block(name, shape, tokens, n_gpus):
     return {"workload": f"{name}: E={shape.n_experts} top-{shape.top_k} H={shape.hidden} "
                         f"I={shape.inter} local=[{shape.local_start},{shape.local_start + shape.n_local}) "
@@ -242,8 +255,13 @@ def config_block(name, shape, tokens, n_gpus):
                         if shape.router.startswith("reference") else
                         "NVFP4 (e2m1, e4m3 block-16 scales, fp32 global scale) from N(0,0.02)"),
             "activations": "bf16 N(0,1)", "l2": "flushed by a 512 MiB write before every timed call",
-            "parallelism": (f"ep{n_gpus}: experts split in contiguous blocks, tokens replicated, "
-                            "fp32 shares summed over NVLink peer memory") if n_gpus > 1 else "single GPU"}
+            "parallelism": ("single GPU" if n_gpus == 1 else
+                            f"ep{n_gpus}: experts split in contiguous blocks, tokens split evenly over the "
+                            "ranks, token rows dispatched over NVLink peer memory to the ranks owning "
+                            "their experts, fp32 shares of those ranks summed back over NVLink"
+                            if name in PREFILL_WORKLOADS else
+                            f"ep{n_gpus}: experts split in contiguous blocks, tokens replicated, "
+                            "fp32 shares summed over NVLink peer memory")}
 
 
 # ----------------------------------------------------------------------------- reference arm
@@ -385,23 +403,30 @@ class Bench:
         shape = sweep(synth, name, None, self.args.experts if name == self.args.workload else None)[0]
         w = make_weights(synth, shape, dev)
         moe = None
+        sharded = world > 1 and name in PREFILL_WORKLOADS
         if world > 1:
             # expert-parallel: this rank repacks and computes only its block of experts; every
-            # rank holds all tokens (decode layout); the exchange runs over NVLink peer memory
+            # rank holds all tokens (decode layout) or its slice of them (prefill layout); the
+            # exchanges run over NVLink peer memory
             from muse_moe_w4a16_b200 import ep
             moe = ep.ExpertParallelMoE(w)
-            moe.reserve_decode(max(tokens), shape.hidden, dev)   # before any graph is captured
-            layer_call = moe.forward_replicated
+            if sharded:
+                layer_call = moe.forward_sharded
+            else:
+                moe.reserve_decode(max(tokens), shape.hidden, dev)   # before any graph is captured
+                layer_call = moe.forward_replicated
             n_local = len(moe.experts)
         else:
             state = pkg.prepare(w)
             layer_call = lambda d: pkg.kernel_fn(d, state)  # noqa: E731
             n_local = shape.n_local
         inputs = {t: make_input(synth, shape, name, t) for t in tokens}
+        # what this rank's calls see: the whole batch, or its slice of it (prefill layout)
+        run_in = {t: shard(inputs[t], self.rank, world) for t in tokens} if sharded else inputs
 
         graphs, outs, dev_in = {}, {}, {}
         for t in tokens:
-            d = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in inputs[t].items()}
+            d = {k: (v.to(dev) if isinstance(v, torch.Tensor) else v) for k, v in run_in[t].items()}
             dev_in[t] = d
             outs[t] = layer_call(d)          # eager first call (kernel attributes, exchange buffers)
             torch.cuda.synchronize()
@@ -409,11 +434,17 @@ class Bench:
                 g = torch.cuda.CUDAGraph()
                 with torch.cuda.graph(g):
                     outs[t] = layer_call(d)
+            elif sharded:
+                g = _Eager(lambda d=d: layer_call(d))   # millisecond calls: launch cost is noise
             else:
                 g = moe.decode_graphs(d)
             graphs[t] = g
 
-        parity = self.parity_ep(shape, w, tokens, dev_in, graphs) if (full and world > 1) else None
+        parity = None
+        if full and sharded:
+            parity = self.parity_sharded(w, tokens, dev_in, layer_call)
+        elif full and world > 1:
+            parity = self.parity_ep(shape, w, tokens, dev_in, graphs)
         w_np = numpy_weights(w) if (full and world == 1 and not args.no_cpu_baseline) else None
         del w
 
@@ -444,12 +475,12 @@ class Bench:
         res = {"name": name, "shape": shape, "tokens": tokens, "per_t": per_t, "inputs": inputs,
                "n_local": n_local, "clocks": clocks, "parity": parity}
         if full:
-            res["e2e"] = self.e2e(inputs, shape, tokens, layer_call)
+            res["e2e"] = self.e2e(run_in, shape, tokens, layer_call)
         if full and world == 1:
             res["ref_style"] = self.reference_style(graphs, tokens)
         if world == 1:
             res["stage_us"] = self.stages(tokens, dev_in, state, outs)
-        elif full:
+        elif full and not sharded:
             res["rank_split"] = self.rank_split(tokens, dev_in, moe)
         del graphs
         torch.cuda.synchronize()
@@ -503,6 +534,29 @@ class Bench:
                            "every rank's bits against rank 0's",
                 "tol": PARITY_TOL, "per_T": rows, "ok": bool(flag.item())}
 
+    def parity_sharded(self, w, tokens, dev_in, layer_call):
+        """Prefill layout: every rank's rows against the single-GPU layer on the same tokens
+        (all experts, computed on that rank); the worst rank's figures."""
+        from oracle import moe_oracle as orc
+        pkg = self.pkg
+        state = pkg.prepare(w)
+        rows, all_ok = {}, True
+        for t in tokens:
+            got = layer_call(dev_in[t])
+            single = pkg.kernel_fn(dev_in[t], state)
+            torch.cuda.synchronize()
+            ok, _, err, worst = orc.compare(bits(got), bits(single), PARITY_TOL)
+            r = gather_ranks(self.world, [float(err), float(worst), 1.0 if ok else 0.0])
+            row = {"rel_l2": max(x[0] for x in r), "worst_row": max(x[1] for x in r),
+                   "ok": all(x[2] == 1.0 for x in r)}
+            all_ok &= row["ok"]
+            rows[str(t)] = row
+        del state
+        torch.cuda.empty_cache()
+        self._lib.device_status(reset=True)
+        return {"against": "single-GPU layer on each rank's own tokens (pinned to the CPU oracle by the "
+                           "tests); worst rank", "tol": PARITY_TOL, "per_T": rows, "ok": all_ok}
+
     # -- extra passes -----------------------------------------------------------------------
 
     def e2e(self, inputs, shape, tokens, layer_call):
@@ -511,11 +565,12 @@ class Bench:
         args, world, dev, stream = self.args, self.world, self.dev, self.stream
         h2d = sum(inputs[t][k].numel() * inputs[t][k].element_size()
                   for t in tokens for k in ("hidden_states", "topk_ids", "topk_weights"))
-        d2h = sum(t * shape.hidden * 2 for t in tokens)
+        rows = {t: inputs[t]["hidden_states"].shape[0] for t in tokens}   # this rank's tokens
+        d2h = sum(rows[t] * shape.hidden * 2 for t in tokens)
         per_t = []
         for t in tokens:
             hi = {k: (v.pin_memory() if isinstance(v, torch.Tensor) else v) for k, v in inputs[t].items()}
-            ho = torch.empty((t, shape.hidden), dtype=torch.bfloat16).pin_memory()
+            ho = torch.empty((rows[t], shape.hidden), dtype=torch.bfloat16).pin_memory()
             d = {k: (torch.empty_like(v, device=dev) if isinstance(v, torch.Tensor) else v) for k, v in hi.items()}
             for k in ("hidden_states", "topk_ids", "topk_weights"):
                 d[k].copy_(hi[k], non_blocking=True)
@@ -691,12 +746,21 @@ def run_muse(args, world, rank, local):
             roof_peak = pk["hbm_gbs"]
             roof_kernel = roof_kernel.format("bytes")
     else:
-        # whole expert-parallel call: every rank's algorithmic bytes over the slowest rank's
-        # time, against N GPUs' bandwidth
-        achieved = sum(r["bytes"] for r in per_rows) / (sum(per_t) * 1e-6) / 1e9
+        # whole expert-parallel call: the work of every rank over the slowest rank's time,
+        # against N GPUs' peak -- FLOPs for a tensor-bound (prefill) sweep, else bytes
+        flops = sum(r["flops"] for r in per_rows)
+        nbytes = sum(r["bytes"] for r in per_rows)
+        if flops / (pk["bf16_tflops_sustained"] * 1e12) > nbytes / (pk["hbm_gbs"] * 1e9):
+            bound, unit = "tensor", "TFLOP/s"
+            achieved = flops / (sum(per_t) * 1e-6) / 1e12
+            roof_peak = pk["bf16_tflops_sustained"] * world
+            what = f"{world} x the sustained bf16 peak"
+        else:
+            achieved = nbytes / (sum(per_t) * 1e-6) / 1e9
+            roof_peak = pk["hbm_gbs"] * world
+            what = f"{world} x HBM peak"
         roof_kernel = (f"whole expert-parallel layer call over {world} GPUs (local layer kernels + "
-                       f"peer-memory exchange), sweep aggregate, against {world} x HBM peak")
-        roof_peak = pk["hbm_gbs"] * world
+                       f"peer-memory exchanges), sweep aggregate, against {what}")
     tr = traffic_record(args.workload) if world == 1 else None
     line = {
         "metric": metric_name(args.workload), "value": round(geomean(per_t), 3), "unit": "us/call",
