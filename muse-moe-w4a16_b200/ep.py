@@ -235,6 +235,11 @@ class ExpertParallelMoE:
             mine = torch.empty((t_r, part.shape[1]), dtype=part.dtype, device=part.device)
             dist.reduce_scatter_tensor(mine, part, op=dist.ReduceOp.SUM, group=self.group)
             return self._cast(mine)
+        if x.dtype != torch.bfloat16 or x.dim() != 2 or tuple(ids.shape) != tuple(wts.shape) or ids.shape[0] != t_r:
+            # checked before the dispatch signals the peers: a call that fails later leaves the
+            # ranks out of step (see check_status)
+            raise _lib.MuseError(_lib.MUSE_ERR_INVALID_ARGUMENT,
+                                 "hidden_states must be bf16 [T_r, H] with topk_ids / topk_weights [T_r, K]")
         H, K = x.shape[1], ids.shape[1]
         self._peer_buffers(R * t_r * H, x.device)
         recv = self._recv_buffers(R * t_r, H, K, x.device)
