@@ -998,6 +998,18 @@ int pick_stages(int n_box, bool pair, int* b_stages) {
   const int P = pick_pipes(n_box, pair);
   const Geo g = make_geo(pipe_cols(P), n_box, 1, 1, pair);
   const size_t budget = (226u * 1024u - sizeof(SharedCtl) - 1024) / P;
+  if (pair) {
+    // Pair items (prefill, tensor-bound): the MMAs of a chunk read 64 KiB of activation rows,
+    // refetched from L2 for every weight tile, so the activation ring gets three slots and the
+    // weights what is left (measured at cfg5 T=4096 / 8192: 4368 / 8108 us against 4780 / 8824
+    // with eight weight slots and two activation slots; weight tiles are few and mostly L2 hits
+    // by then).
+    for (int sw = kMaxStages; sw >= 2; --sw)
+      if (sw * (size_t)kWStageBytes + 3 * (size_t)g.b_bytes <= budget) {
+        *b_stages = 3;
+        return sw;
+      }
+  }
   for (int sw = kMaxStages; sw >= 2; --sw) {
     for (int extra = 1; extra >= (pair ? 2 - sw : 0); --extra) {
       const int sb = sw + extra;
