@@ -228,6 +228,32 @@ int muse_moe_peer_exchange_bf16(const uint64_t* shares0, const uint64_t* shares1
                                 void* out, muse_stream_t stream);
 
 /*
+ * One expert-parallel decode call of this rank, layer and exchange together: this rank's fp32
+ * share of the layer (its local experts, as muse_moe_forward_partial; n_experts as in
+ * muse_moe_forward_ex) is written into its share buffer of the call's parity,
+ * (expect_parity ? shares1 : shares0)[rank], and every rank's share is then summed into bf16
+ * `out` [tokens, hidden] exactly as muse_moe_peer_exchange_bf16 does in `mode` (0 or 2), with
+ * the same buffers, flags, generation count, parity check and wait limit. When the layer is a
+ * single cooperative launch (small batches; muse_moe_launch_plan_ex path 2) and mode is 0, the
+ * exchange runs inside that launch after its combine -- its last block to finish the combine
+ * signals the peers, every block waits for them and sums its part -- so the call is one
+ * launch; otherwise it is the layer's launches followed by the exchange kernel. The output bits
+ * are the same either way. expect_parity must be 0 or 1 (it names the share buffer). Replaces
+ * the ep8 rank's layer plus the all-reduce of the ranks' partial outputs (reference.py:18-22,
+ * TASK.md:29).
+ */
+int muse_moe_forward_exchange_bf16(const void* x, const int32_t* topk_ids, const float* topk_weights,
+                                   int tokens, int top_k, int local_start, int local_count,
+                                   int n_experts, int hidden, int inter, const uint8_t* w13p,
+                                   const uint8_t* w13_sfp, const float* w13_gs, const uint8_t* w2p,
+                                   const uint8_t* w2_sfp, const float* w2_gs, const void* post_norm_w,
+                                   void* workspace, size_t workspace_bytes, const uint64_t* shares0,
+                                   const uint64_t* shares1, const uint64_t* flags,
+                                   const uint64_t* staging, int ranks, int rank, int mode,
+                                   int expect_parity, long long timeout_us, void* out,
+                                   muse_stream_t stream);
+
+/*
  * The prefill-layout exchange (tokens split over the ranks, ranks x n_per_rank elements in every
  * share): out (bf16 [n_per_rank], this rank) = sum over ranks r, in order, of elements
  * [rank * n_per_rank, (rank + 1) * n_per_rank) of rank r's share -- this rank's tokens. Same

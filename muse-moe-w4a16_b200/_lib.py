@@ -45,6 +45,11 @@ SIGNATURES: dict[str, tuple] = {
     "muse_moe_peer_exchange_bf16": (_I, [ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
                                          ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
                                          _I, _I, ctypes.c_size_t, _I, _I, ctypes.c_longlong, _P, _P]),
+    "muse_moe_forward_exchange_bf16": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, _I, _I,
+                                            _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_size_t,
+                                            ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
+                                            ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
+                                            _I, _I, _I, _I, ctypes.c_longlong, _P, _P]),
     "muse_moe_ep_dispatch": (_I, [_P, _P, _P, _I, _I, _I, _I, _I, ctypes.POINTER(_I),
                                   ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),
                                   ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64),

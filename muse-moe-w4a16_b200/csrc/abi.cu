@@ -5,6 +5,7 @@
 #include "common.cuh"
 #include "kernels.cuh"
 #include "layout.cuh"
+#include "peer.cuh"
 
 namespace muse {
 namespace {
@@ -200,7 +201,8 @@ int forward_impl(const void* x, const int32_t* topk_ids, const float* topk_weigh
                  const uint8_t* w13p, const uint8_t* w13_sfp, const float* w13_gs,
                  const uint8_t* w2p, const uint8_t* w2_sfp, const float* w2_gs,
                  const void* post_norm_w, void* out, void* workspace, size_t workspace_bytes,
-                 cudaStream_t st, cudaEvent_t* ev, bool f32_out = false, int n_experts = 0) {
+                 cudaStream_t st, cudaEvent_t* ev, bool f32_out = false, int n_experts = 0,
+                 const ExchangeArgs* ex = nullptr) {
   int rc = check_dims(tokens, top_k, local_start, local_count, hidden, inter);
   if (rc) return rc;
   if (n_experts == 0) n_experts = local_count;
@@ -309,6 +311,7 @@ int forward_impl(const void* x, const int32_t* topk_ids, const float* topk_weigh
     g.topk_weights = topk_weights;
     g.out = out;
     g.out_f32 = f32_out;
+    if (ex) g.ex = *ex;
     if ((rc = mark(1))) return rc;
     if ((rc = launch_expert_gemm(tmap_xs, tmap_x, tmap_i, g, st))) return rc;
     if ((rc = mark(2))) return rc;
@@ -387,6 +390,54 @@ extern "C" int muse_moe_forward_partial(const void* x, const int32_t* topk_ids,
   return forward_impl(x, topk_ids, topk_weights, tokens, top_k, local_start, local_count, hidden,
                       inter, w13p, w13_sfp, w13_gs, w2p, w2_sfp, w2_gs, post_norm_w, out_f32,
                       workspace, workspace_bytes, (cudaStream_t)stream, nullptr, true);
+}
+
+extern "C" int muse_moe_forward_exchange_bf16(
+    const void* x, const int32_t* topk_ids, const float* topk_weights, int tokens, int top_k,
+    int local_start, int local_count, int n_experts, int hidden, int inter, const uint8_t* w13p,
+    const uint8_t* w13_sfp, const float* w13_gs, const uint8_t* w2p, const uint8_t* w2_sfp,
+    const float* w2_gs, const void* post_norm_w, void* workspace, size_t workspace_bytes,
+    const uint64_t* shares0, const uint64_t* shares1, const uint64_t* flags, const uint64_t* staging,
+    int ranks, int rank, int mode, int expect_parity, long long timeout_us, void* out,
+    muse_stream_t stream) {
+  if (!shares0 || !shares1 || !flags || !out || ranks < 1 || ranks > kMaxPeers || rank < 0 ||
+      rank >= ranks || (mode != 0 && mode != 2) || (expect_parity != 0 && expect_parity != 1) ||
+      timeout_us < 0 || tokens < 0 || hidden <= 0 || reinterpret_cast<uintptr_t>(out) % 16)
+    return MUSE_ERR_INVALID_ARGUMENT;
+  ExchangeArgs ex{};
+  for (int r = 0; r < ranks; ++r) {
+    if (!shares0[r] || !shares1[r] || !flags[r] || shares0[r] % 16 || shares1[r] % 16 || flags[r] % 4)
+      return MUSE_ERR_INVALID_ARGUMENT;
+    ex.share[0][r] = reinterpret_cast<const float*>(shares0[r]);
+    ex.share[1][r] = reinterpret_cast<const float*>(shares1[r]);
+    ex.flags[r] = reinterpret_cast<uint32_t*>(flags[r]);
+  }
+  float* share = const_cast<float*>(ex.share[expect_parity][rank]);
+  const size_t n = (size_t)tokens * hidden;
+  const int n_eff = n_experts == 0 ? local_count : n_experts;
+  // One launch when the layer is the single cooperative launch and the one-round sum is asked
+  // for: the exchange follows the combine inside it. Otherwise the layer, then the exchange kernel.
+  const bool fused = mode == 0 && tokens > 0 && local_count > 0 && n_eff >= local_count &&
+                     check_dims(tokens, top_k, local_start, local_count, hidden, inter) == MUSE_OK &&
+                     path_of(tokens, top_k, n_eff) == 2;
+  if (fused) {
+    ex.out = static_cast<uint16_t*>(out);
+    ex.n4 = n / 4;
+    ex.timeout_ns = timeout_us ? (unsigned long long)timeout_us * 1000ull : kDefaultTimeoutNs;
+    ex.ranks = ranks;
+    ex.rank = rank;
+    ex.expect_parity = expect_parity;
+    return forward_impl(x, topk_ids, topk_weights, tokens, top_k, local_start, local_count, hidden,
+                        inter, w13p, w13_sfp, w13_gs, w2p, w2_sfp, w2_gs, post_norm_w, share, workspace,
+                        workspace_bytes, (cudaStream_t)stream, nullptr, true, n_experts, &ex);
+  }
+  const int rc = forward_impl(x, topk_ids, topk_weights, tokens, top_k, local_start, local_count,
+                              hidden, inter, w13p, w13_sfp, w13_gs, w2p, w2_sfp, w2_gs, post_norm_w,
+                              share, workspace, workspace_bytes, (cudaStream_t)stream, nullptr, true,
+                              n_experts);
+  if (rc) return rc;
+  return muse_moe_peer_exchange_bf16(shares0, shares1, flags, staging, ranks, rank, n, mode,
+                                     expect_parity, timeout_us, out, stream);
 }
 
 extern "C" int muse_moe_cast_bf16(const float* in, void* out, size_t n, muse_stream_t stream) {

@@ -30,6 +30,7 @@
 #include "combine.cuh"
 #include "kernels.cuh"
 #include "layout.cuh"
+#include "peer.cuh"
 #include "ptx.cuh"
 #include "route.cuh"
 #include "trace.cuh"
@@ -90,6 +91,9 @@ struct SharedCtl {
   uint8_t slot_of_row[kMaxInlinePairs];  // route_inline: top-k slot of each pair row
   int c_row[kMaxTopK], c_key[kMaxTopK], c_order[kMaxTopK], c_srow[kMaxTopK], c_n;  // combine of one token
   float c_coef[kMaxTopK], c_scoef[kMaxTopK];
+  ExchangeArgs ex;                   // the decode exchange after the combine: its arguments,
+  uint32_t ex_gen;                   // its generation
+  int ex_ok;                         // and this block's go / no-go
 };
 
 // Per-launch geometry shared by all roles.
@@ -943,6 +947,14 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
   if (threadIdx.x == 0) MUSE_TRACE_AT(3);
   if (warp == kMmaWarp0) ptx::tmem_dealloc(tbase, kTmemCols);
   if (kFused && a.fused) combine_tokens(ctl, a, n_local);
+  // expert-parallel decode: every rank's share summed into this rank's bf16 output
+  // (its arguments are read from shared memory: a reference into the kernel's parameters would
+  // make the compiler copy all of them to the stack)
+  if (kFused && a.ex.ranks > 0) {
+    if (threadIdx.x == 0) ctl.ex = a.ex;
+    __syncthreads();
+    grid_exchange_one_round(ctl.ex, a.error_flag, &ctl.ex_gen, &ctl.ex_ok);
+  }
   if (threadIdx.x == 0) MUSE_TRACE_AT(4);
 }
 

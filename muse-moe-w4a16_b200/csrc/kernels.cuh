@@ -57,6 +57,22 @@ struct PhaseArgs {
   int wait_target;
 };
 
+// Ranks of an expert-parallel exchange.
+constexpr int kMaxPeers = 8;
+
+// Expert-parallel decode in the single launch: after the combine has written this rank's fp32
+// share (the launch's `out`), the one-round exchange of peer.cuh sums every rank's share into
+// bf16 `out` here. Pointers of other ranks are peer mappings of their symmetric buffers.
+struct ExchangeArgs {
+  const float* share[2][kMaxPeers];  // share buffers of parity 0 / 1 of rank r
+  uint32_t* flags[kMaxPeers];        // flag array of rank r
+  uint16_t* out;                     // bf16 [n], this rank's memory
+  size_t n4;                         // elements of a share / 4
+  unsigned long long timeout_ns;
+  int ranks;                         // 0: no exchange
+  int rank, expect_parity;
+};
+
 // Arguments of one expert-GEMM launch. A launch runs one phase (a plain GEMM) or, for small
 // batches, both GEMMs and the combine of the whole layer call (`fused`).
 struct GemmArgs {
@@ -88,6 +104,7 @@ struct GemmArgs {
   const float* topk_weights;
   void* out;
   int out_f32;
+  ExchangeArgs ex;         // fused: the decode exchange after the combine (ex.ranks 0: none)
 };
 
 // Largest batch (tokens x top_k) whose routing the first GEMM does in its own prologue, and

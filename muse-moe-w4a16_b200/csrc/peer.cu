@@ -47,20 +47,11 @@
 // all ranks) before the next call.
 #include "common.cuh"
 #include "kernels.cuh"
+#include "peer.cuh"
 #include "ptx.cuh"
 
 namespace muse {
 namespace {
-
-constexpr int kMaxPeers = 8;
-constexpr int kRound2 = 8;          // slots [8, 16): round-2 signals
-constexpr int kGenSlot = 16;        // calls completed
-constexpr int kDoneA = 17;          // blocks past step 3 (two-round) in the current call
-constexpr int kDoneB = 18;          // blocks finished in the current call
-constexpr int kFail = 19;           // a wait of the current call expired
-constexpr int kDispatch = 20;       // slots [20, 28): prefill dispatch signals
-constexpr int kDispDone = 28;       // dispatch blocks finished in the current call
-constexpr unsigned long long kDefaultTimeoutNs = 1000000000ull;  // 1 s
 
 enum Mode { kAllReduce1 = 0, kReduceScatter = 1, kAllReduce2 = 2, kRoutedScatter = 3 };
 
@@ -78,54 +69,8 @@ struct PeerArgs {
   int h4;                            // mode 3: float4 groups per token row
 };
 
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned long long global_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Wait (one thread) until slots [base, base + ranks) of `mine` hold at least gen. Gives up after
-// timeout_ns, or as soon as another block of this rank has recorded a failure.
-__device__ bool wait_slots(const uint32_t* mine, int base, int ranks, uint32_t gen,
-                           unsigned long long timeout_ns) {
-  const unsigned long long t0 = global_ns();
-  for (int r = 0; r < ranks; ++r) {
-    unsigned ns = 32;
-    while (ld_acquire_sys(mine + base + r) < gen) {
-      if (global_ns() - t0 > timeout_ns) return false;
-      if (*reinterpret_cast<const volatile uint32_t*>(mine + kFail)) return false;
-      __nanosleep(ns);
-      if (ns < 256) ns <<= 1;
-    }
-  }
-  return true;
-}
-
 __device__ __forceinline__ uint2 sum_bf16x4(const PeerArgs& a, int par, size_t i4) {
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int r = 0; r < a.ranks; ++r) {
-    const float4 v = __ldcv(reinterpret_cast<const float4*>(a.share[par][r]) + i4);
-    acc.x += v.x;
-    acc.y += v.y;
-    acc.z += v.z;
-    acc.w += v.w;
-  }
-  __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
-  __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
-  uint2 packed;
-  packed.x = *reinterpret_cast<uint32_t*>(&lo);
-  packed.y = *reinterpret_cast<uint32_t*>(&hi);
-  return packed;
+  return rank_sum_bf16x4(a.share[par], a.ranks, i4);
 }
 
 // Mode 3: this rank's token t, float4 group c: the sum over the ranks in the token's mask.

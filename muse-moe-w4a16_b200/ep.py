@@ -46,7 +46,7 @@ import torch
 import torch.distributed as dist
 
 from . import _lib
-from .layer import Inputs, Weights, cast_bf16, kernel_fn_partial, prepare
+from .layer import Inputs, Weights, cast_bf16, kernel_fn_exchange, kernel_fn_partial, prepare
 
 
 def expert_block(n_experts: int, rank: int, world: int) -> range:
@@ -130,20 +130,25 @@ class ExpertParallelMoE:
 
     def _decode(self, local: Inputs, parity: int, stage_events: list | None = None) -> torch.Tensor:
         """The rank's share written into its share buffer `parity`, then the peer exchange (the
-        kernel takes the generation from the device and checks it has this parity)."""
+        kernel takes the generation from the device and checks it has this parity). One library
+        call -- for small batches one launch, the exchange inside the layer's single launch --
+        unless stage events are asked for, which need the layer and the exchange apart."""
         x = local["hidden_states"]
         T, H = x.shape
         peer = self._peer
         share = peer["buf"][parity * peer["cap"]:parity * peer["cap"] + T * H].view(T, H)
-        if stage_events:
-            stage_events[0].record()
+        mode = self.exchange_mode(T * H)
+        if not stage_events:
+            return kernel_fn_exchange(local, self.state, share, {
+                "shares0": peer["shares"][0], "shares1": peer["shares"][1], "flags": peer["flags"],
+                "staging": peer["staging"], "ranks": self.world, "rank": self.rank,
+                "mode": mode, "parity": parity, "timeout_us": self.timeout_us})
+        stage_events[0].record()
         kernel_fn_partial(local, self.state, out=share)
-        if stage_events:
-            stage_events[1].record()
+        stage_events[1].record()
         out = torch.empty((T, H), dtype=torch.bfloat16, device=x.device)
-        self._exchange(T * H, self.exchange_mode(T * H), parity, out)
-        if stage_events:
-            stage_events[2].record()
+        self._exchange(T * H, mode, parity, out)
+        stage_events[2].record()
         return out
 
     def _exchange(self, n: int, mode: int, parity: int, out: torch.Tensor) -> None:

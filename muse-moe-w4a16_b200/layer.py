@@ -172,6 +172,30 @@ def kernel_fn_partial(data: Inputs, state: dict, out: torch.Tensor | None = None
     return out
 
 
+def kernel_fn_exchange(data: Inputs, state: dict, share: torch.Tensor, exchange: dict,
+                       out: torch.Tensor | None = None,
+                       workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """One expert-parallel decode call of this rank (muse_moe_forward_exchange_bf16): this
+    rank's fp32 share of the layer (kernel_fn_partial's value) is written into `share` -- the
+    rank's share buffer of the call's parity, fp32 [T, H] -- and every rank's share is summed
+    into bf16 [T, H]. `exchange` holds the exchange's arguments: shares0, shares1, flags,
+    staging (ctypes uint64 arrays of the ranks' buffer addresses), ranks, rank, mode (0 or 2),
+    parity (of `share`) and timeout_us. Small batches run it as one launch."""
+    args, share = _call_args(data, state, share, workspace, torch.float32)
+    T, H = share.shape
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.bfloat16, device=share.device)
+    elif out.dtype != torch.bfloat16 or tuple(out.shape) != (T, H) or not out.is_contiguous():
+        raise _lib.MuseError(_lib.MUSE_ERR_INVALID_ARGUMENT, f"out must be a contiguous bfloat16 [{T}, {H}]")
+    # args: x, ids, wts, T, K, lo, cnt, n_experts, H, I, 6 weight pointers, post_norm_w, out,
+    # out_f32, workspace, workspace bytes, stream, events
+    ex = exchange
+    _lib.call("muse_moe_forward_exchange_bf16", *args[:17], args[19], args[20],
+              ex["shares0"], ex["shares1"], ex["flags"], ex["staging"], ex["ranks"], ex["rank"],
+              ex["mode"], ex["parity"], int(ex.get("timeout_us", 0)), _ptr(out), args[21])
+    return out
+
+
 def cast_bf16(x: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
     """bf16 copy of a contiguous fp32 CUDA tensor (numel a multiple of 8), on the current stream."""
     _require_cuda(x, "x")

@@ -148,6 +148,30 @@ def test_peer_allreduce_rejects_bad_arguments(lib):
     assert f(u64(0x1004, 0x2000), s1, flags, 2, 0, 64, out, None) == bad  # misaligned share
 
 
+def test_forward_exchange_rejects_bad_arguments(lib):
+    """The layer-plus-exchange call checks its exchange arguments before any device work: the
+    share buffer it writes is named by expect_parity, so the parity must be 0 or 1; the exchange
+    modes of the decode layout are 0 and 2."""
+    from muse_moe_w4a16_b200 import _lib
+    u64 = ctypes.c_uint64 * 2
+    s0, s1, flags = u64(0x1000, 0x2000), u64(0x1100, 0x2100), u64(0x3000, 0x4000)
+    f = lib.muse_moe_forward_exchange_bf16
+    bad = _lib.MUSE_ERR_INVALID_ARGUMENT
+    layer = [None] * 3 + [1, 8, 0, 8, 16, 256, 256] + [None] * 7 + [None, 0]
+
+    def call(shares0=s0, ranks=2, rank=0, mode=0, parity=1, out=0x5000):
+        return f(*layer, shares0, s1, flags, None, ranks, rank, mode, parity, 0, out, None)
+
+    assert call(rank=2) == bad                    # rank out of range
+    assert call(ranks=9) == bad                   # more than 8 ranks
+    assert call(parity=-1) == bad                 # the share buffer must be named
+    assert call(mode=1) == bad                    # not a decode-layout mode
+    assert call(out=None) == bad                  # no output
+    assert call(out=0x5004) == bad                # misaligned output
+    assert call(shares0=u64(0x1000, 0)) == bad    # null peer share
+    assert call(shares0=u64(0x1008, 0x2000)) == bad   # misaligned share
+
+
 def test_launch_plan_counts_only_local_pairs_per_expert(pkg):
     """On an expert-parallel slice the token tile follows the pairs a local expert can expect
     (T*K / model experts), not T*K / local experts: the reference problem's ep8 slice at bs 256
