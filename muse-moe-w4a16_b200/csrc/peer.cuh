@@ -72,38 +72,47 @@ __device__ __forceinline__ uint2 rank_sum_bf16x4(const float* const* share, int 
 }
 
 // The one-round exchange run by every block of a cooperative grid after the grid has written
-// this rank's share (ex.share[p][ex.rank], p = the call's parity): the grid's last block to
-// arrive signals round 1 to every rank, every block waits (bounded) for all ranks' signals and
-// sums its part of the elements into ex.out, and the last block out advances the generation.
-// The same steps and the same sums as peer_exchange_kernel in mode 0, so the bits are the same
-// as the layer launch followed by that kernel. s_gen / s_ok: shared-memory words of the block.
+// this rank's share (ex.share[p][ex.rank], p = the call's parity): every block counts itself in
+// once its share stores are visible on this GPU, and the last one, after a system-scope fence,
+// signals round 1 to every rank. Only as many blocks as the sum needs (one float4 group per
+// thread) then wait (bounded) for all ranks' signals, sum their part of the elements into ex.out
+// and count themselves out; the last of them advances the generation. The others return. The
+// same sums as peer_exchange_kernel in mode 0, so the bits are the same as the layer launch
+// followed by that kernel. s_gen / s_ok: shared-memory words of the block.
 // Not inlined: it runs once, at the end of the layer kernel, and kept out of line it leaves the
 // register allocation of the kernel's loops alone.
 static __device__ __noinline__ void grid_exchange_one_round(const ExchangeArgs& ex, int* error_flag,
                                                                uint32_t* s_gen, int* s_ok) {
   uint32_t* mine = ex.flags[ex.rank];
+  const size_t want = (ex.n4 + blockDim.x - 1) / blockDim.x;
+  const unsigned summers = want == 0 ? 1u : (want < gridDim.x ? (unsigned)want : gridDim.x);
   __syncthreads();  // this block's share stores are issued
   if (threadIdx.x == 0) {
-    // read before this block counts itself: the generation advances only after every block has
-    // counted itself out below
+    // read before this block counts itself in: the generation advances only after the summing
+    // blocks have counted themselves out, which follows every block's count-in
     const uint32_t gen = *reinterpret_cast<volatile uint32_t*>(mine + kGenSlot) + 1u;
     *s_gen = gen;
     int ok = (int)(gen & 1u) == ex.expect_parity;
     if (!ok) {
       if (blockIdx.x == 0) atomicExch(error_flag, 7);   // the share went to the other buffer
     } else {
-      __threadfence_system();
+      __threadfence();
       if (atomicAdd(mine + kDoneA, 1u) == gridDim.x - 1) {
         mine[kDoneA] = 0;
+        __threadfence_system();   // every block's share stores before the peers hear of them
         for (int r = 0; r < ex.ranks; ++r) st_release_sys(ex.flags[r] + ex.rank, gen);
       }
-      ok = wait_slots(mine, 0, ex.ranks, gen, ex.timeout_ns) ? 1 : 2;
-      if (ok == 2) {
-        atomicExch(mine + kFail, 1u);
-        atomicExch(error_flag, 6);
+      if (blockIdx.x < summers) {
+        ok = wait_slots(mine, 0, ex.ranks, gen, ex.timeout_ns) ? 1 : 2;
+        if (ok == 2) {
+          atomicExch(mine + kFail, 1u);
+          atomicExch(error_flag, 6);
+        }
+      } else {
+        ok = 3;   // counted in; takes no part in the sum
       }
     }
-    *s_ok = ok;   // 0: parity mismatch (nothing done), 1: go, 2: a wait expired
+    *s_ok = ok;   // 0: parity mismatch (nothing done), 1: sum, 2: a wait expired, 3: done
   }
   __syncthreads();
   const uint32_t gen = *s_gen;
@@ -111,14 +120,14 @@ static __device__ __noinline__ void grid_exchange_one_round(const ExchangeArgs& 
   if (ok == 1) {
     const float* const* share = ex.share[gen & 1u];
     uint2* out = reinterpret_cast<uint2*>(ex.out);
-    const size_t stride = (size_t)gridDim.x * blockDim.x;
+    const size_t stride = (size_t)summers * blockDim.x;
     for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < ex.n4; i += stride)
       out[i] = rank_sum_bf16x4(share, ex.ranks, i);
   }
   __syncthreads();
-  if (threadIdx.x == 0 && ok != 0) {
+  if (threadIdx.x == 0 && (ok == 1 || ok == 2)) {
     __threadfence();
-    if (atomicAdd(mine + kDoneB, 1u) == gridDim.x - 1) {
+    if (atomicAdd(mine + kDoneB, 1u) == summers - 1) {
       mine[kDoneB] = 0;
       const bool failed = *reinterpret_cast<volatile uint32_t*>(mine + kFail) != 0;
       mine[kFail] = 0;
