@@ -95,8 +95,13 @@ int path_of(int tokens, int top_k, int n_experts) {
 }
 
 // Phases with more K chunks than this split each item over the pipelines; shorter ones give
-// each item to one pipeline (unless the kernel finds fewer than 4 items per CTA).
-constexpr int kSplitKMinChunks = 8;
+// each item to one pipeline (unless the kernel finds fewer than 4 items per CTA). The single
+// launch splits from 9 chunks on, the separate GEMM launches from 17 (measured on one B200,
+// L2 flushed: 16 instead of 8 for the separate launches takes cfg4 T=32 / 256 from 917 / 1422
+// to 909 / 1409 us -- GEMM2's 16-chunk items stay whole -- and leaves cfg2, cfg3 and cfg0
+// unchanged; for the single launch it costs cfg2 T=16 2.5 %; 64 slows cfg0's 32-chunk items).
+constexpr int kSplitKMinChunksFused = 8;
+constexpr int kSplitKMinChunks = 16;
 
 PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
 
@@ -278,7 +283,8 @@ int forward_impl(const void* x, const int32_t* topk_ids, const float* topk_weigh
   gemm1.gs = w13_gs;
   gemm1.mode = 1;
   gemm1.ld_out = inter;
-  gemm1.split_k = gemm1.k_chunks > kSplitKMinChunks;
+  const int split_min = path == 2 ? kSplitKMinChunksFused : kSplitKMinChunks;
+  gemm1.split_k = gemm1.k_chunks > split_min;
   PhaseArgs gemm2{};
   gemm2.m_tiles = hidden / kTileM;
   gemm2.k_chunks = inter / kChunkK;
@@ -287,7 +293,7 @@ int forward_impl(const void* x, const int32_t* topk_ids, const float* topk_weigh
   gemm2.gs = w2_gs;
   gemm2.mode = 2;
   gemm2.ld_out = hidden;
-  gemm2.split_k = gemm2.k_chunks > kSplitKMinChunks;
+  gemm2.split_k = gemm2.k_chunks > split_min;
 
   if ((rc = mark(0))) return rc;
   if (path == 2) {
