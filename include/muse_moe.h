@@ -234,8 +234,9 @@ int muse_moe_peer_exchange_bf16(const uint64_t* shares0, const uint64_t* shares1
  * (expect_parity ? shares1 : shares0)[rank], and every rank's share is then summed into bf16
  * `out` [tokens, hidden] exactly as muse_moe_peer_exchange_bf16 does in `mode` (0 or 2), with
  * the same buffers, flags, generation count, parity check and wait limit. When the layer is a
- * single cooperative launch (small batches; muse_moe_launch_plan_ex path 2) and mode is 0, the
- * exchange runs inside that launch after its combine -- its last block to finish the combine
+ * single cooperative launch (small batches; muse_moe_launch_plan_ex path 2), mode is 0 and at
+ * most two ranks take part (measured faster there; slower from four), the exchange runs inside
+ * that launch after its combine -- its last block to finish the combine
  * signals the peers, every block waits for them and sums its part -- so the call is one
  * launch; otherwise it is the layer's launches followed by the exchange kernel. The output bits
  * are the same either way. expect_parity must be 0 or 1 (it names the share buffer). Replaces

@@ -398,6 +398,13 @@ extern "C" int muse_moe_forward_partial(const void* x, const int32_t* topk_ids,
                       workspace, workspace_bytes, (cudaStream_t)stream, nullptr, true);
 }
 
+// Ranks up to which the decode exchange runs inside the layer's single launch. Measured with
+// CUDA graphs at cfg4 T=1 (max over ranks): 2 ranks 78 us inside against 83 us as a second
+// launch; 4 ranks 65.6 against 62.1 (the exchange kernel's 7 blocks start as soon as the layer
+// launch ends, while in the fused tail every block of the grid counts in before the peers are
+// signalled, and a few blocks make all the peer reads).
+constexpr int kMaxFusedExchangeRanks = 2;
+
 extern "C" int muse_moe_forward_exchange_bf16(
     const void* x, const int32_t* topk_ids, const float* topk_weights, int tokens, int top_k,
     int local_start, int local_count, int n_experts, int hidden, int inter, const uint8_t* w13p,
@@ -421,9 +428,11 @@ extern "C" int muse_moe_forward_exchange_bf16(
   float* share = const_cast<float*>(ex.share[expect_parity][rank]);
   const size_t n = (size_t)tokens * hidden;
   const int n_eff = n_experts == 0 ? local_count : n_experts;
-  // One launch when the layer is the single cooperative launch and the one-round sum is asked
-  // for: the exchange follows the combine inside it. Otherwise the layer, then the exchange kernel.
-  const bool fused = mode == 0 && tokens > 0 && local_count > 0 && n_eff >= local_count &&
+  // One launch when the layer is the single cooperative launch, the one-round sum is asked for
+  // and at most kMaxFusedExchangeRanks ranks take part: the exchange follows the combine inside
+  // it. Otherwise the layer, then the exchange kernel.
+  const bool fused = mode == 0 && ranks <= kMaxFusedExchangeRanks && tokens > 0 && local_count > 0 &&
+                     n_eff >= local_count &&
                      check_dims(tokens, top_k, local_start, local_count, hidden, inter) == MUSE_OK &&
                      path_of(tokens, top_k, n_eff) == 2;
   if (fused) {

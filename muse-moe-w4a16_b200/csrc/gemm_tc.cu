@@ -93,7 +93,7 @@ struct SharedCtl {
   float c_coef[kMaxTopK], c_scoef[kMaxTopK];
   ExchangeArgs ex;                   // the decode exchange after the combine: its arguments,
   uint32_t ex_gen;                   // its generation
-  int ex_ok;                         // and this block's go / no-go
+  int ex_ok[2];                      // and this block's go / no-go (count-in, then sum)
 };
 
 // Per-launch geometry shared by all roles.
@@ -953,7 +953,7 @@ expert_gemm_tc(const __grid_constant__ CUtensorMap tmap_b, const __grid_constant
   if (kFused && a.ex.ranks > 0) {
     if (threadIdx.x == 0) ctl.ex = a.ex;
     __syncthreads();
-    grid_exchange_one_round(ctl.ex, a.error_flag, &ctl.ex_gen, &ctl.ex_ok);
+    grid_exchange_one_round(ctl.ex, a.error_flag, &ctl.ex_gen, ctl.ex_ok);
   }
   if (threadIdx.x == 0) MUSE_TRACE_AT(4);
 }

@@ -93,7 +93,7 @@ __device__ __forceinline__ uint2 routed_sum_bf16x4(const PeerArgs& a, int par, s
 }
 
 __global__ void __launch_bounds__(256) peer_exchange_kernel(const PeerArgs a) {
-  __shared__ int s_ok;
+  __shared__ int s_ok, s_last;
   __shared__ uint32_t s_gen;
   uint32_t* mine = a.flags[a.rank];
   if (threadIdx.x == 0) s_gen = *reinterpret_cast<volatile uint32_t*>(mine + kGenSlot) + 1u;
@@ -140,15 +140,24 @@ __global__ void __launch_bounds__(256) peer_exchange_kernel(const PeerArgs a) {
     }
   }
   if (a.mode == kAllReduce2) {
-    // step 4: once every block of this rank has written its part of the slice, tell the peers
+    // step 4: once every block of this rank has written its part of the slice, the last one
+    // tells the peers (one thread per rank, so the signals go out in parallel)
     __syncthreads();
     if (threadIdx.x == 0) {
       __threadfence_system();
+      s_last = 0;
       if (atomicAdd(mine + kDoneA, 1u) == gridDim.x - 1) {
         mine[kDoneA] = 0;
-        if (!*reinterpret_cast<volatile uint32_t*>(mine + kFail))
-          for (int r = 0; r < a.ranks; ++r) st_release_sys(a.flags[r] + kRound2 + a.rank, gen);
+        __threadfence();
+        s_last = !*reinterpret_cast<volatile uint32_t*>(mine + kFail);
       }
+    }
+    __syncthreads();
+    if (s_last && threadIdx.x < a.ranks) {
+      __threadfence_system();
+      st_release_sys(a.flags[threadIdx.x] + kRound2 + a.rank, gen);
+    }
+    if (threadIdx.x == 0) {
       if (s_ok) {
         s_ok = wait_slots(mine, kRound2, a.ranks, gen, a.timeout_ns);
         if (!s_ok) {
@@ -203,6 +212,7 @@ struct DispatchArgs {
 __global__ void __launch_bounds__(256) ep_dispatch_kernel(const DispatchArgs a) {
   __shared__ uint32_t s_mask;
   __shared__ uint32_t s_gen;
+  __shared__ int s_last;
   uint32_t* mine = a.flags[a.rank];
   if (threadIdx.x == 0) s_gen = *reinterpret_cast<volatile uint32_t*>(mine + kGenSlot) + 1u;
   for (int t = blockIdx.x; t < a.tokens; t += gridDim.x) {
@@ -230,17 +240,25 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const DispatchArgs a) 
     }
   }
   __syncthreads();
+  const uint32_t gen = s_gen;
   if (threadIdx.x == 0) {
-    const uint32_t gen = s_gen;
     __threadfence_system();
+    s_last = 0;
     if (atomicAdd(mine + kDispDone, 1u) == gridDim.x - 1) {
       mine[kDispDone] = 0;
-      for (int r = 0; r < a.ranks; ++r) st_release_sys(a.flags[r] + kDispatch + a.rank, gen);
-      if (!wait_slots(mine, kDispatch, a.ranks, gen, a.timeout_ns)) {
-        atomicExch(mine + kFail, 1u);
-        atomicExch(a.error_flag, 6);
-      }
+      __threadfence();
+      s_last = 1;
     }
+  }
+  __syncthreads();
+  if (!s_last) return;
+  if (threadIdx.x < a.ranks) {   // the last block: one thread per rank signals, in parallel
+    __threadfence_system();
+    st_release_sys(a.flags[threadIdx.x] + kDispatch + a.rank, gen);
+  }
+  if (threadIdx.x == 0 && !wait_slots(mine, kDispatch, a.ranks, gen, a.timeout_ns)) {
+    atomicExch(mine + kFail, 1u);
+    atomicExch(a.error_flag, 6);
   }
 }
 

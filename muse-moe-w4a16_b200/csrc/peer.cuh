@@ -73,12 +73,12 @@ __device__ __forceinline__ uint2 rank_sum_bf16x4(const float* const* share, int 
 
 // The one-round exchange run by every block of a cooperative grid after the grid has written
 // this rank's share (ex.share[p][ex.rank], p = the call's parity): every block counts itself in
-// once its share stores are visible on this GPU, and the last one, after a system-scope fence,
-// signals round 1 to every rank. Only as many blocks as the sum needs (one float4 group per
+// once its share stores are visible on this GPU, and the last one signals round 1 to every
+// rank, one thread per rank, each after a system-scope fence. Only as many blocks as the sum needs (one float4 group per
 // thread) then wait (bounded) for all ranks' signals, sum their part of the elements into ex.out
 // and count themselves out; the last of them advances the generation. The others return. The
 // same sums as peer_exchange_kernel in mode 0, so the bits are the same as the layer launch
-// followed by that kernel. s_gen / s_ok: shared-memory words of the block.
+// followed by that kernel. s_gen, s_ok[2]: shared-memory words of the block.
 // Not inlined: it runs once, at the end of the layer kernel, and kept out of line it leaves the
 // register allocation of the kernel's loops alone.
 static __device__ __noinline__ void grid_exchange_one_round(const ExchangeArgs& ex, int* error_flag,
@@ -97,13 +97,25 @@ static __device__ __noinline__ void grid_exchange_one_round(const ExchangeArgs& 
       if (blockIdx.x == 0) atomicExch(error_flag, 7);   // the share went to the other buffer
     } else {
       __threadfence();
-      if (atomicAdd(mine + kDoneA, 1u) == gridDim.x - 1) {
+      if (atomicAdd(mine + kDoneA, 1u) == gridDim.x - 1) {   // the last block in signals
         mine[kDoneA] = 0;
-        __threadfence_system();   // every block's share stores before the peers hear of them
-        for (int r = 0; r < ex.ranks; ++r) st_release_sys(ex.flags[r] + ex.rank, gen);
+        __threadfence();
+        ok |= 4;
       }
+    }
+    s_ok[0] = ok;
+  }
+  __syncthreads();
+  if ((s_ok[0] & 4) && threadIdx.x < ex.ranks) {
+    // one thread per rank: the signals go out in parallel
+    __threadfence_system();   // every block's share stores before the peers hear of them
+    st_release_sys(ex.flags[threadIdx.x] + ex.rank, *s_gen);
+  }
+  if (threadIdx.x == 0) {
+    int ok = s_ok[0] & 3;
+    if (ok == 1) {
       if (blockIdx.x < summers) {
-        ok = wait_slots(mine, 0, ex.ranks, gen, ex.timeout_ns) ? 1 : 2;
+        ok = wait_slots(mine, 0, ex.ranks, *s_gen, ex.timeout_ns) ? 1 : 2;
         if (ok == 2) {
           atomicExch(mine + kFail, 1u);
           atomicExch(error_flag, 6);
@@ -112,11 +124,11 @@ static __device__ __noinline__ void grid_exchange_one_round(const ExchangeArgs& 
         ok = 3;   // counted in; takes no part in the sum
       }
     }
-    *s_ok = ok;   // 0: parity mismatch (nothing done), 1: sum, 2: a wait expired, 3: done
+    s_ok[1] = ok;   // 0: parity mismatch (nothing done), 1: sum, 2: a wait expired, 3: done
   }
   __syncthreads();
   const uint32_t gen = *s_gen;
-  const int ok = *s_ok;
+  const int ok = s_ok[1];
   if (ok == 1) {
     const float* const* share = ex.share[gen & 1u];
     uint2* out = reinterpret_cast<uint2*>(ex.out);
