@@ -100,6 +100,10 @@ def test_host_path_refuses_cpu_tensors(pkg):
     d = synth.baseline_input(shape, 3, seed=0)
     with pytest.raises(pkg.MuseError):
         pkg.kernel_fn(d, {"inter": 128, "hidden": 128, "n_experts": 4})
+    from muse_moe_w4a16_b200 import layer
+    with pytest.raises(pkg.MuseError):   # the layer-plus-exchange call checks the same way
+        layer.kernel_fn_exchange(d, {"inter": 128, "hidden": 128, "n_experts": 4},
+                                 torch.zeros(3, 128), {})
 
 
 def test_product_path_does_not_import_oracle():
